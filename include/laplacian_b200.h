@@ -1,0 +1,175 @@
+/*
+ * laplacian_b200.h — C ABI of the B200 (sm_100a) LaplacianFormer operators.
+ *
+ * Plain pointers, sizes and a CUDA stream; no framework types.  Every tensor
+ * is dense, row-major and lives in device memory of the current CUDA device.
+ * Calls are asynchronous on `stream` (0 = legacy default stream), never
+ * allocate memory and never synchronise.  Each entry point returns LF_OK or
+ * one of the LF_ERR_* codes; lf_last_error() returns a message for the most
+ * recent failure on the calling host thread.
+ *
+ * Layouts follow the reference operators (BirdWithDreams/LaplacianFormer):
+ *   query  Q   [bh, n, d]      (the reference's [B,H,N,D], bh = B*H)
+ *   key    KT  [bh, d, m]      (the reference's [B,H,D,M]: landmarks transposed,
+ *                               src/LaplaceSubtraction_cuda.cu:25-27, :62)
+ *   output S   [bh, n, m]
+ *   matrices   [batch, n, n]   (the reference's [B,H,N,N], batch = B*H)
+ *
+ * The reference binds its operators with pybind11 (src/wrapper.cpp:73-98);
+ * each entry point below names the reference function it replaces.
+ */
+#ifndef LAPLACIAN_B200_H
+#define LAPLACIAN_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define LF_API __attribute__((visibility("default")))
+#else
+#define LF_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* lf_stream_t; /* == cudaStream_t */
+
+/* Element types (all operands of one call share it). */
+enum lf_dtype {
+    LF_F32 = 0,
+    LF_F64 = 1,
+    LF_F16 = 2,
+    LF_BF16 = 3
+};
+
+/* Status codes. */
+enum lf_status {
+    LF_OK = 0,
+    LF_ERR_INVALID = 1,      /* bad pointer, size or stride                  */
+    LF_ERR_DTYPE = 2,        /* element type not supported by this operator  */
+    LF_ERR_UNSUPPORTED = 3,  /* size outside the supported range             */
+    LF_ERR_CUDA = 4,         /* a CUDA runtime call or launch failed         */
+    LF_ERR_TIMEOUT = 5       /* a device-side bounded wait expired           */
+};
+
+/* NewtonInverse initialisation modes. */
+enum lf_ns_init {
+    /* P = A + reg*I, V0 = 1.8 / (max_i sum_j P_ij)^2 * P
+       (src/NewtonInverse_cuda_kernel.cu:82-120, :169, :176-178). */
+    LF_NS_INIT_REFERENCE = 0,
+    /* P = A + reg*I, X0 = P^T / (||P||_1 ||P||_inf). */
+    LF_NS_INIT_SCALED_TRANSPOSE = 1
+};
+
+/* NewtonInverse arithmetic for fp32 / fp16 / bf16 inputs. */
+enum lf_ns_precision {
+    /* Every product on tcgen05 tensor cores as hi*hi + hi*lo + lo*hi fp16
+       parts with fp32 accumulation (about 22 significant bits). */
+    LF_NS_PREC_SPLIT3 = 0,
+    /* Single fp16 product for all but the last two iterations, split
+       products for the last two (Newton–Schulz corrects earlier rounding). */
+    LF_NS_PREC_MIXED = 1,
+    /* CUDA-core fp32 FMA for every product (no tensor cores). */
+    LF_NS_PREC_FP32_SIMT = 2
+};
+
+/* ---------------------------------------------------------------------- */
+/* Library information                                                     */
+/* ---------------------------------------------------------------------- */
+
+/* Message describing the last failure on this host thread ("" if none). */
+LF_API const char* lf_last_error(void);
+/* CUDART_VERSION the library was built with.
+   Replaces laplace::get_cudart_version (src/cuda_version.cu:7-26). */
+LF_API int lf_cudart_version(void);
+/* Library version as major*10000 + minor*100 + patch. */
+LF_API int lf_version(void);
+
+/* ---------------------------------------------------------------------- */
+/* LaplaceSubtraction                                                      */
+/* ---------------------------------------------------------------------- */
+
+/* S[b,i,j] = sum_c |Q[b,i,c] - KT[b,c,j]|.  dtype: F32, F64, F16, BF16.
+   Replaces laplace::LaplaceSubtraction_forward_cuda
+   (src/LaplaceSubtraction_cuda.cu:55-67 -> src/LaplaceSubtraction_cuda_kernel.cu:455-485). */
+LF_API int lf_laplace_sub_fwd(const void* q, const void* kT, void* s,
+                       int64_t bh, int64_t n, int64_t m, int64_t d,
+                       int dtype, lf_stream_t stream);
+
+/* dQ[b,i,c] = sum_j G[b,i,j] * sign(Q[b,i,c] - KT[b,c,j]), sign(0) = 0.
+   Replaces laplace::LaplaceSubtraction_backward_query_cuda
+   (src/LaplaceSubtraction_cuda.cu:69-84 -> src/LaplaceSubtraction_cuda_kernel.cu:487-547). */
+LF_API int lf_laplace_sub_bwd_query(const void* g, const void* q, const void* kT, void* dq,
+                             int64_t bh, int64_t n, int64_t m, int64_t d,
+                             int dtype, lf_stream_t stream);
+
+/* dKT[b,c,j] = -sum_i G[b,i,j] * sign(Q[b,i,c] - KT[b,c,j]).
+   Replaces laplace::LaplaceSubtraction_backward_key_cuda
+   (src/LaplaceSubtraction_cuda.cu:86-101 -> src/LaplaceSubtraction_cuda_kernel.cu:549-609). */
+LF_API int lf_laplace_sub_bwd_key(const void* g, const void* q, const void* kT, void* dkT,
+                           int64_t bh, int64_t n, int64_t m, int64_t d,
+                           int dtype, lf_stream_t stream);
+
+/* Both gradients from one pass over G; either output may be NULL.  Has no
+   single counterpart in the reference, which reads G once per gradient
+   (src/LaplaceSubtraction_cuda_kernel.cu:487-609). */
+LF_API int lf_laplace_sub_bwd(const void* g, const void* q, const void* kT,
+                       void* dq, void* dkT,
+                       int64_t bh, int64_t n, int64_t m, int64_t d,
+                       int dtype, lf_stream_t stream);
+
+/* Legacy forward with the reference's per-output tree reduction in the
+   storage type, including its behaviour for d that is not a power of two.
+   Replaces laplace::LaplaceSubtraction_reduce_forward_cuda
+   (src/LaplaceSubtraction_cuda.cu:103-116 -> src/LaplaceSubtraction_cuda_kernel.cu:611-647). */
+LF_API int lf_laplace_sub_reduce_fwd(const void* q, const void* kT, void* s,
+                              int64_t bh, int64_t n, int64_t m, int64_t d,
+                              int dtype, lf_stream_t stream);
+
+/* ---------------------------------------------------------------------- */
+/* NewtonInverse                                                           */
+/* ---------------------------------------------------------------------- */
+
+/* 1 if n is supported by lf_newton_inverse_fwd / _bwd, else 0.
+   Replaces laplace::NewtonInverse_supports (src/NewtonInverse_cuda_kernel.cu:753-762). */
+LF_API int lf_newton_inverse_supported(int64_t n);
+
+/* Reference semantics: P = A + 0.01 I, V0 = alpha P, `iters` steps of
+   V <- 2V - V P V.  dtype: F32, F64, F16, BF16.
+   Replaces laplace::NewtonInverse_forward_cuda (src/NewtonInverse_cuda_kernel.cu:764-794). */
+LF_API int lf_newton_inverse_fwd(const void* a, void* x, int64_t batch, int64_t n, int iters,
+                          int dtype, lf_stream_t stream);
+
+/* Extended forward: init mode (lf_ns_init), diagonal regulariser `reg` and
+   arithmetic (lf_ns_precision).  lf_newton_inverse_fwd(...) is
+   lf_newton_inverse_fwd_ex(..., LF_NS_INIT_REFERENCE, 0.01, LF_NS_PREC_SPLIT3, ...).
+   No counterpart in the reference, whose constants are hard-coded
+   (src/NewtonInverse_cuda_kernel.cu:116, :169). */
+LF_API int lf_newton_inverse_fwd_ex(const void* a, void* x, int64_t batch, int64_t n, int iters,
+                             int dtype, int init_mode, double reg, int precision,
+                             lf_stream_t stream);
+
+/* dA = -(V^T G V^T) for the inverse V and upstream gradient G.
+   Replaces laplace::NewtonInverse_backward_cuda (src/NewtonInverse_cuda_kernel.cu:796-833). */
+LF_API int lf_newton_inverse_bwd(const void* g, const void* v, void* da,
+                          int64_t batch, int64_t n, int dtype, lf_stream_t stream);
+
+/* res[b] = ||(A_b + reg I) X_b - I||_F in fp32 (fp64 for F64 input), the
+   per-matrix residual the batched benchmark reports.  No counterpart in the
+   reference. */
+LF_API int lf_newton_inverse_residual(const void* a, const void* x, void* res,
+                               int64_t batch, int64_t n, double reg,
+                               int dtype, lf_stream_t stream);
+
+/* Synchronises the current device and returns the status word that kernels
+   set when a bounded device-side wait expires (LF_OK if none); clear != 0
+   resets it.  No counterpart in the reference, which can only printf launch
+   errors (src/NewtonInverse_cuda_kernel.cu:790-793). */
+LF_API int lf_device_status(int clear);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LAPLACIAN_B200_H */

@@ -1,0 +1,666 @@
+// LaplaceSubtraction on B200 (sm_100a): pairwise L1 distance between queries
+// and landmarks, its two gradients, and the reference's legacy reduce path.
+//
+//   S[b,i,j]   = sum_c |Q[b,i,c] - KT[b,c,j]|                (forward)
+//   dQ[b,i,c]  =  sum_j G[b,i,j] * sign(Q[b,i,c] - KT[b,c,j])  (backward, query)
+//   dKT[b,c,j] = -sum_i G[b,i,j] * sign(Q[b,i,c] - KT[b,c,j])  (backward, key)
+//
+// Semantics follow src/LaplaceSubtraction_cuda_kernel.cu of the reference
+// (forward :47-141, backward-query :148-267, backward-key :274-393, reduce
+// :399-447).  An L1 distance is not a contraction, so these kernels run on
+// the CUDA cores; the design targets the FP32 issue rate and HBM:
+//
+// * Forward: lanes own query rows, a thread keeps TM rows x 16 channels of
+//   Q in registers and a chunk of MC landmarks' accumulators; landmark values
+//   are warp-uniform broadcasts from shared memory (one 128-bit LDS per four
+//   channels).  Each output is accumulated over the channels in order, with
+//   the same fp32 operations as the reference, so fp32/fp64 results are
+//   bit-identical to the reference kernel.
+// * Backward (fused): lanes own channels, a warp walks query rows and keeps
+//   KT[c, j] and the dKT partials of its chunk of landmarks in registers, so
+//   both reductions are thread-local.  sign(q-k)*g costs one FFMA.SAT
+//   (t = sat(d*2^125 + 0.5) in {0, 1/2, 1}, sign = 2t - 1 exactly):
+//       dQ  = sum_j 2g*t - sum_j g,    dKT = sum_i g - sum_i 2g*t.
+//   The CTAs that split one (b,h) along the rows form a thread-block cluster
+//   and add their dKT partials through distributed shared memory; no atomics
+//   in global memory and no pre-zeroed output.
+#include <cooperative_groups.h>
+
+#include "lf_common.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace lfb {
+namespace {
+
+constexpr int kThreads = 256;
+
+// ---------------------------------------------------------------------------
+// Forward
+// ---------------------------------------------------------------------------
+template <typename T>
+__device__ __forceinline__ void load_chunk16(const T* __restrict__ src, int valid, bool vec,
+                                             typename Elem<T>::acc (&out)[16]) {
+    using A = typename Elem<T>::acc;
+    if (vec && valid >= 16) {
+        if constexpr (sizeof(T) == 4) {
+            const float4* p = reinterpret_cast<const float4*>(src);
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+                float4 x = __ldg(p + v);
+                out[4 * v + 0] = x.x; out[4 * v + 1] = x.y; out[4 * v + 2] = x.z; out[4 * v + 3] = x.w;
+            }
+            return;
+        } else if constexpr (sizeof(T) == 2) {
+            const uint4* p = reinterpret_cast<const uint4*>(src);
+#pragma unroll
+            for (int v = 0; v < 2; ++v) {
+                uint4 x = __ldg(p + v);
+                const T* h = reinterpret_cast<const T*>(&x);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) out[8 * v + e] = Elem<T>::load(h[e]);
+            }
+            return;
+        }
+    }
+#pragma unroll
+    for (int e = 0; e < 16; ++e) out[e] = (e < valid) ? Elem<T>::load(src[e]) : A(0);
+}
+
+template <typename A>
+__device__ __forceinline__ A absdiff_acc(A acc, A q, A k) {
+    if constexpr (sizeof(A) == 4) {
+        return add_abs_ftz(acc, sub_ftz(q, k));
+    } else {
+        A d = q - k;
+        return acc + fabs(d);
+    }
+}
+
+// One CTA = kThreads*TM query rows of one (b,h); thread t owns rows
+// base + t + kThreads*r.  ks holds KT transposed to [m][DP] in the
+// accumulation type (DP = d rounded up to 16, zero padded).
+template <typename T, int TM, int MC>
+__global__ void __launch_bounds__(kThreads)
+lsub_fwd_kernel(const T* __restrict__ q, const T* __restrict__ kT, T* __restrict__ s,
+                int n, int m, int d, int tiles_per_bh, bool vec) {
+    using A = typename Elem<T>::acc;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    A* ks = reinterpret_cast<A*>(smem_raw);
+    const int DP = (d + 15) & ~15;
+    const int MP = ((m + MC - 1) / MC) * MC;
+
+    const int bh = blockIdx.x / tiles_per_bh;
+    const int tile = blockIdx.x - bh * tiles_per_bh;
+    const T* Kb = kT + (int64_t)bh * d * m;
+
+    // Stage KT[bh] (d x m, row-major) transposed into ks[j][c].
+    for (int e = threadIdx.x; e < MP * DP; e += kThreads) {
+        int j = e / DP, c = e - j * DP;
+        ks[e] = (j < m && c < d) ? Elem<T>::load(Kb[(int64_t)c * m + j]) : A(0);
+    }
+    __syncthreads();
+
+    const int64_t row0 = (int64_t)tile * (kThreads * TM) + threadIdx.x;
+    const T* Qb = q + (int64_t)bh * n * d;
+    T* Sb = s + (int64_t)bh * n * m;
+
+    for (int mc = 0; mc < m; mc += MC) {
+        A acc[TM][MC];
+#pragma unroll
+        for (int r = 0; r < TM; ++r)
+#pragma unroll
+            for (int j = 0; j < MC; ++j) acc[r][j] = A(0);
+
+        for (int dc = 0; dc < d; dc += 16) {
+            A qr[TM][16];
+            const int valid = d - dc;
+#pragma unroll
+            for (int r = 0; r < TM; ++r) {
+                int64_t row = row0 + (int64_t)kThreads * r;
+                if (row < n) {
+                    load_chunk16<T>(Qb + row * d + dc, valid, vec, qr[r]);
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) qr[r][e] = A(0);
+                }
+            }
+            // Padded channels (c >= d) hold 0 in both operands: |0 - 0| adds +0.
+            const int cmax = valid < 16 ? valid : 16;
+#pragma unroll
+            for (int j = 0; j < MC; ++j) {
+                const A* kr = ks + (mc + j) * DP + dc;
+#pragma unroll
+                for (int c4 = 0; c4 < 4; ++c4) {
+                    if (c4 * 4 >= cmax) break;
+                    A kv[4];
+                    if constexpr (sizeof(A) == 4) {
+                        float4 t = *reinterpret_cast<const float4*>(kr + 4 * c4);
+                        kv[0] = t.x; kv[1] = t.y; kv[2] = t.z; kv[3] = t.w;
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) kv[e] = kr[4 * c4 + e];
+                    }
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        if (4 * c4 + e < cmax) {
+#pragma unroll
+                            for (int r = 0; r < TM; ++r) acc[r][j] = absdiff_acc<A>(acc[r][j], qr[r][4 * c4 + e], kv[e]);
+                        }
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < TM; ++r) {
+            int64_t row = row0 + (int64_t)kThreads * r;
+            if (row >= n) continue;
+            T* out = Sb + row * m + mc;
+#pragma unroll
+            for (int j = 0; j < MC; ++j)
+                if (mc + j < m) out[j] = Elem<T>::store(acc[r][j]);
+        }
+    }
+}
+
+// Landmark chunk per thread: the MC in 4..8 that pads m the least.
+int pick_mc(int64_t m) {
+    int best = 8;
+    int64_t best_pad = ((m + 7) / 8) * 8;
+    for (int c = 7; c >= 4; --c) {
+        int64_t pad = ((m + c - 1) / c) * c;
+        if (pad < best_pad) { best = c; best_pad = pad; }
+    }
+    return best;
+}
+
+template <typename T, int TM, int MC>
+int launch_fwd_mc(const T* q, const T* kT, T* s, int64_t bh, int64_t n, int64_t m, int64_t d,
+                  cudaStream_t st) {
+    using A = typename Elem<T>::acc;
+    const int DP = (int)((d + 15) & ~15);
+    const int MP = (int)(((m + MC - 1) / MC) * MC);
+    size_t smem = (size_t)MP * DP * sizeof(A);
+    if (smem > (size_t)max_optin_smem()) {
+        set_error("LaplaceSubtraction forward: m*d = %lld*%lld needs %zu bytes of shared memory",
+                  (long long)m, (long long)d, smem);
+        return LF_ERR_UNSUPPORTED;
+    }
+    auto kern = lsub_fwd_kernel<T, TM, MC>;
+    if (smem > 48 * 1024)
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    int tiles = (int)((n + kThreads * TM - 1) / (kThreads * TM));
+    int64_t blocks = bh * tiles;
+    if (blocks > 0x7fffffff) { set_error("too many blocks"); return LF_ERR_UNSUPPORTED; }
+    bool vec = (d % 16 == 0) && aligned(q, 16);
+    kern<<<(unsigned)blocks, kThreads, smem, st>>>(q, kT, s, (int)n, (int)m, (int)d, tiles, vec);
+    return check_launch("lsub_fwd_kernel");
+}
+
+template <typename T>
+int launch_fwd(const void* q, const void* kT, void* s, int64_t bh, int64_t n, int64_t m, int64_t d,
+               cudaStream_t st) {
+    const T* Q = static_cast<const T*>(q);
+    const T* K = static_cast<const T*>(kT);
+    T* S = static_cast<T*>(s);
+    constexpr int TM = sizeof(T) == 8 ? 1 : 2;
+    switch (pick_mc(m)) {
+        case 4: return launch_fwd_mc<T, TM, 4>(Q, K, S, bh, n, m, d, st);
+        case 5: return launch_fwd_mc<T, TM, 5>(Q, K, S, bh, n, m, d, st);
+        case 6: return launch_fwd_mc<T, TM, 6>(Q, K, S, bh, n, m, d, st);
+        case 7: return launch_fwd_mc<T, TM, 7>(Q, K, S, bh, n, m, d, st);
+        default: return launch_fwd_mc<T, TM, 8>(Q, K, S, bh, n, m, d, st);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Fused backward
+// ---------------------------------------------------------------------------
+template <typename A>
+__device__ __forceinline__ A step_of(A q, A k) {
+    if constexpr (sizeof(A) == 4) {
+        return half_step_ftz(sub_ftz(q, k));
+    } else {
+        A d = q - k;
+        return d > A(0) ? A(1) : (d < A(0) ? A(0) : A(0.5));
+    }
+}
+
+constexpr int kRowChunk = 32;  // query rows staged per pass
+
+struct BwdGeom {
+    int n, m, d;
+    int DB, MCN, RG;  // channel blocks (32 lanes), landmark chunks, row groups
+    int MP;           // landmark stride of the staged gradient tile
+    int KSTR;         // row stride of the per-CTA dKT accumulator (odd, conflict free)
+    int rows_per_cta;
+};
+
+// grid = (cs, bh), cluster = (cs, 1, 1).  CTA x of (b,h) handles query rows
+// [x*rows_per_cta, (x+1)*rows_per_cta).  Warp w works on channel block
+// w % DB, landmark chunk (w / DB) % MCN and row group w / (DB*MCN).
+template <typename T, int MB, bool DQ, bool DK>
+__global__ void __launch_bounds__(kThreads, (DQ && sizeof(T) != 8) ? 2 : 1)
+lsub_bwd_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* __restrict__ kT,
+                T* __restrict__ dq, T* __restrict__ dk, BwdGeom geo) {
+    using A = typename Elem<T>::acc;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int n = geo.n, m = geo.m, d = geo.d;
+    const int MP = geo.MP;
+    // Shared memory carve-up (accumulation type):
+    //   gs   [kRowChunk][MP]   2*G of the staged rows (zero padded)
+    //   rsum [kRowChunk]       sum_j G of each staged row
+    //   dqb  [kRowChunk][d]    dQ partials when MCN > 1
+    //   csum [MP]              sum_i G of the CTA's rows, per landmark
+    //   dkb  [d][KSTR]         dKT partials of this CTA
+    A* gs = reinterpret_cast<A*>(smem_raw);
+    A* rsum = gs + kRowChunk * MP;
+    A* dqb = rsum + kRowChunk;
+    A* csum = dqb + (geo.MCN > 1 ? kRowChunk * d : 0);
+    A* dkb = csum + MP;
+
+    cg::cluster_group cluster = cg::this_cluster();
+    const int bh = blockIdx.y;
+    const int split = blockIdx.x;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int groups = geo.DB * geo.MCN;
+    const int db = warp % geo.DB;
+    const int mcb = (warp / geo.DB) % geo.MCN;
+    const int rg = warp / groups;
+    const bool warp_active = rg < geo.RG;
+    const int c = db * 32 + lane;
+    const bool lane_active = warp_active && c < d;
+    const int j0 = mcb * MB;
+
+    const T* Gb = g + (int64_t)bh * n * m;
+    const T* Qb = q + (int64_t)bh * n * d;
+    const T* Kb = kT + (int64_t)bh * d * m;
+
+    if (DK) {
+        for (int e = threadIdx.x; e < d * geo.KSTR; e += kThreads) dkb[e] = A(0);
+        for (int e = threadIdx.x; e < MP; e += kThreads) csum[e] = A(0);
+    }
+
+    // Landmark values of this lane's channel and its dKT partials.
+    A kreg[MB];
+    A dka[MB];
+#pragma unroll
+    for (int jj = 0; jj < MB; ++jj) {
+        int j = j0 + jj;
+        kreg[jj] = (lane_active && j < m) ? Elem<T>::load(Kb[(int64_t)c * m + j]) : A(0);
+        dka[jj] = A(0);
+    }
+
+    const int64_t r_begin = (int64_t)split * geo.rows_per_cta;
+    const int64_t r_end = (r_begin + geo.rows_per_cta < (int64_t)n) ? r_begin + geo.rows_per_cta : (int64_t)n;
+
+    for (int64_t rc = r_begin; rc < r_end; rc += kRowChunk) {
+        const int rows = (int)((r_end - rc) < kRowChunk ? (r_end - rc) : kRowChunk);
+        __syncthreads();  // previous chunk fully consumed
+        // Stage 2*G for the chunk (coalesced over the contiguous rows*m block).
+        const T* gsrc = Gb + rc * m;
+        for (int e = threadIdx.x; e < kRowChunk * MP; e += kThreads) {
+            int i = e / MP, j = e - i * MP;
+            A v = (i < rows && j < m) ? Elem<T>::load(gsrc[(int64_t)i * m + j]) : A(0);
+            gs[e] = v + v;
+        }
+        if (DQ && geo.MCN > 1)
+            for (int e = threadIdx.x; e < kRowChunk * d; e += kThreads) dqb[e] = A(0);
+        __syncthreads();
+        if (DQ && threadIdx.x < kRowChunk) {
+            A sacc = A(0);
+            for (int j = 0; j < m; ++j) sacc += gs[threadIdx.x * MP + j];
+            rsum[threadIdx.x] = sacc * A(0.5);
+        }
+        if (DK) {
+            for (int j = threadIdx.x; j < m; j += kThreads) {
+                A sacc = A(0);
+                for (int i = 0; i < rows; ++i) sacc += gs[i * MP + j];
+                csum[j] += sacc * A(0.5);
+            }
+        }
+        __syncthreads();
+
+        if (lane_active) {
+#pragma unroll 1
+            for (int i = rg; i < rows; i += geo.RG) {
+                const A qv = Elem<T>::load(Qb[(rc + i) * d + c]);
+                const A* grow = gs + i * MP + j0;
+                A dqa = A(0);
+#pragma unroll
+                for (int j4 = 0; j4 < MB; j4 += 4) {
+                    A gv[4];
+                    if constexpr (sizeof(A) == 4) {
+                        float4 t4 = *reinterpret_cast<const float4*>(grow + j4);
+                        gv[0] = t4.x; gv[1] = t4.y; gv[2] = t4.z; gv[3] = t4.w;
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) gv[e] = grow[j4 + e];
+                    }
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const A t = step_of<A>(qv, kreg[j4 + e]);
+                        if (DQ) dqa = fma(gv[e], t, dqa);
+                        if (DK) dka[j4 + e] = fma(gv[e], t, dka[j4 + e]);
+                    }
+                }
+                if (DQ) {
+                    if (geo.MCN == 1) {
+                        dq[((int64_t)bh * n + rc + i) * d + c] = Elem<T>::store(dqa - rsum[i]);
+                    } else {
+                        atomicAdd(&dqb[i * d + c], mcb == 0 ? dqa - rsum[i] : dqa);
+                    }
+                }
+            }
+        }
+        if (DQ && geo.MCN > 1) {
+            __syncthreads();
+            for (int e = threadIdx.x; e < rows * d; e += kThreads)
+                dq[((int64_t)bh * n + rc) * d + e] = Elem<T>::store(dqb[e]);
+        }
+    }
+
+    if (!DK) return;
+
+    // dKT[c][j] = csum[j] - sum_i 2g*t, first within the CTA ...
+    if (lane_active) {
+#pragma unroll
+        for (int jj = 0; jj < MB; ++jj) {
+            int j = j0 + jj;
+            if (j < m) atomicAdd(&dkb[c * geo.KSTR + j], -dka[jj]);
+        }
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < d * m; e += kThreads) {
+        int cc = e / m, j = e - cc * m;
+        dkb[cc * geo.KSTR + j] += csum[j];
+    }
+    // ... then across the cluster through distributed shared memory.
+    cluster.sync();
+    const int cs = (int)cluster.num_blocks();
+    const int rank = (int)cluster.block_rank();
+    const int total = d * m;
+    const int per = (total + cs - 1) / cs;
+    const int e0 = rank * per, e1 = min(total, e0 + per);
+    T* dkout = dk + (int64_t)bh * d * m;
+    for (int e = e0 + threadIdx.x; e < e1; e += kThreads) {
+        int cc = e / m, j = e - cc * m;
+        A sacc = A(0);
+        for (int r = 0; r < cs; ++r) {
+            const A* peer = cluster.map_shared_rank(dkb, r);
+            sacc += peer[cc * geo.KSTR + j];
+        }
+        dkout[e] = Elem<T>::store(sacc);
+    }
+    cluster.sync();  // keep this CTA's shared memory alive until peers are done
+}
+
+// Landmark chunk per warp (MB) and number of chunks (mcn): least padding of m
+// subject to (channel blocks) x (chunks) <= warps per CTA; ties prefer chunks
+// of at most 52 landmarks (larger ones spill registers in the fused kernel),
+// then the larger chunk.
+int pick_mb(int64_t m, int64_t d, int& mcn) {
+    static const int cands[] = {8, 16, 24, 32, 40, 48, 52, 56, 64};
+    const int64_t db = (d + 31) / 32;
+    int best = 0;
+    int64_t best_pad = -1;
+    for (int c : cands) {
+        int64_t chunks = (m + c - 1) / c;
+        if (chunks * db > kThreads / 32) continue;
+        int64_t pad = chunks * c;
+        bool better = best_pad < 0 || pad < best_pad;
+        if (!better && pad == best_pad) {
+            bool c_ok = c <= 52, b_ok = best <= 52;
+            better = (c_ok && !b_ok) || (c_ok == b_ok && c > best);
+        }
+        if (better) { best = c; best_pad = pad; }
+    }
+    mcn = best ? (int)((m + best - 1) / best) : 0;
+    return best;
+}
+
+template <typename T, int MB, bool DQ, bool DK>
+int launch_bwd_mb(const T* g, const T* q, const T* kT, T* dq, T* dk, int64_t bh, int64_t n,
+                  int64_t m, int64_t d, int mcn, cudaStream_t st) {
+    using A = typename Elem<T>::acc;
+    BwdGeom geo;
+    geo.n = (int)n; geo.m = (int)m; geo.d = (int)d;
+    geo.DB = (int)((d + 31) / 32);
+    geo.MCN = mcn;
+    if (geo.DB * geo.MCN > kThreads / 32) {
+        set_error("LaplaceSubtraction backward: d=%lld, m=%lld exceed one CTA's warps", (long long)d, (long long)m);
+        return LF_ERR_UNSUPPORTED;
+    }
+    geo.RG = (kThreads / 32) / (geo.DB * geo.MCN);
+    geo.MP = (int)(((m + 3) / 4) * 4);
+    if (geo.MP < mcn * MB) geo.MP = mcn * MB;
+    geo.KSTR = (int)(m | 1);
+    size_t smem = sizeof(A) * ((size_t)kRowChunk * geo.MP + kRowChunk +
+                               (geo.MCN > 1 ? (size_t)kRowChunk * d : 0) + geo.MP +
+                               (DK ? (size_t)d * geo.KSTR : 0));
+    if (smem > (size_t)max_optin_smem()) {
+        set_error("LaplaceSubtraction backward: needs %zu bytes of shared memory", smem);
+        return LF_ERR_UNSUPPORTED;
+    }
+    // Split each (b,h) over a cluster of up to 8 CTAs along the rows, aiming
+    // for at least two CTAs per SM in total.
+    int sms = num_sms();
+    int64_t want = (2 * (int64_t)sms + bh - 1) / bh;
+    int64_t cs = want < 1 ? 1 : (want > 8 ? 8 : want);
+    int64_t max_by_rows = (n + kRowChunk - 1) / kRowChunk;
+    if (cs > max_by_rows) cs = max_by_rows < 1 ? 1 : max_by_rows;
+    int64_t rpc = (n + cs - 1) / cs;
+    rpc = ((rpc + kRowChunk - 1) / kRowChunk) * kRowChunk;
+    geo.rows_per_cta = (int)rpc;
+    if (bh > 65535) { set_error("b*h = %lld exceeds 65535", (long long)bh); return LF_ERR_UNSUPPORTED; }
+
+    auto kern = lsub_bwd_kernel<T, MB, DQ, DK>;
+    if (smem > 48 * 1024)
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)cs, (unsigned)bh, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)cs;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t err = cudaLaunchKernelEx(&cfg, kern, g, q, kT, dq, dk, geo);
+    if (err != cudaSuccess) {
+        set_error("lsub_bwd_kernel launch: %s", cudaGetErrorString(err));
+        return LF_ERR_CUDA;
+    }
+    return check_launch("lsub_bwd_kernel");
+}
+
+template <typename T, bool DQ, bool DK>
+int launch_bwd_t(const void* g, const void* q, const void* kT, void* dq, void* dk, int64_t bh,
+                 int64_t n, int64_t m, int64_t d, cudaStream_t st) {
+    const T* G = static_cast<const T*>(g);
+    const T* Q = static_cast<const T*>(q);
+    const T* K = static_cast<const T*>(kT);
+    T* DQp = static_cast<T*>(dq);
+    T* DKp = static_cast<T*>(dk);
+    int mcn = 1;
+    int mb = pick_mb(m, d, mcn);
+    if (mb == 0) {
+        set_error("LaplaceSubtraction backward: m=%lld with d=%lld exceeds one CTA (needs ceil(d/32)*ceil(m/64) <= 8)",
+                  (long long)m, (long long)d);
+        return LF_ERR_UNSUPPORTED;
+    }
+#define LF_BWD_CASE(MBV) case MBV: return launch_bwd_mb<T, MBV, DQ, DK>(G, Q, K, DQp, DKp, bh, n, m, d, mcn, st);
+    switch (mb) {
+        LF_BWD_CASE(8) LF_BWD_CASE(16) LF_BWD_CASE(24) LF_BWD_CASE(32) LF_BWD_CASE(40)
+        LF_BWD_CASE(48) LF_BWD_CASE(52) LF_BWD_CASE(56) LF_BWD_CASE(64)
+        default: break;
+    }
+#undef LF_BWD_CASE
+    set_error("internal: no backward tile for m=%lld", (long long)m);
+    return LF_ERR_UNSUPPORTED;
+}
+
+// ---------------------------------------------------------------------------
+// Legacy reduce forward: one warp per output.  Partials follow the
+// reference's thread assignment for blockDim b = min(d, 256) (thread t sums
+// channels t, t+b, ... in the storage type) and its halving tree
+// s[t] += s[t+stride], stride = b/2, b/4, ..., including the partials the
+// tree drops when b is not a power of two (:429-442).
+// ---------------------------------------------------------------------------
+template <typename T>
+struct StoreArith {  // one operation in float, rounded to T (c10::Half semantics)
+    static __device__ __forceinline__ T add(T a, T b) { return T(float(a) + float(b)); }
+    static __device__ __forceinline__ T sub(T a, T b) { return T(float(a) - float(b)); }
+    static __device__ __forceinline__ bool nonneg(T a) { return float(a) >= 0.f; }
+    static __device__ __forceinline__ T neg(T a) { return T(-float(a)); }
+};
+template <> struct StoreArith<float> {
+    static __device__ __forceinline__ float add(float a, float b) { float r; asm("add.rn.ftz.f32 %0,%1,%2;" : "=f"(r) : "f"(a), "f"(b)); return r; }
+    static __device__ __forceinline__ float sub(float a, float b) { return sub_ftz(a, b); }
+    static __device__ __forceinline__ bool nonneg(float a) { return a >= 0.f; }
+    static __device__ __forceinline__ float neg(float a) { return -a; }
+};
+template <> struct StoreArith<double> {
+    static __device__ __forceinline__ double add(double a, double b) { return __dadd_rn(a, b); }
+    static __device__ __forceinline__ double sub(double a, double b) { return __dsub_rn(a, b); }
+    static __device__ __forceinline__ bool nonneg(double a) { return a >= 0.0; }
+    static __device__ __forceinline__ double neg(double a) { return -a; }
+};
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads)
+lsub_reduce_kernel(const T* __restrict__ q, const T* __restrict__ kT, T* __restrict__ s,
+                   int64_t total, int n, int m, int d) {
+    __shared__ T part[kThreads / 32][256];
+    using Ar = StoreArith<T>;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int b = d < 256 ? d : 256;
+    T* sp = part[warp];
+    for (int64_t o = (int64_t)blockIdx.x * (kThreads / 32) + warp; o < total;
+         o += (int64_t)gridDim.x * (kThreads / 32)) {
+        const int64_t per_bh = (int64_t)n * m;
+        const int64_t bhi = o / per_bh;
+        const int64_t rem = o - bhi * per_bh;
+        const int i = (int)(rem / m), j = (int)(rem - (int64_t)(rem / m) * m);
+        const T* qr = q + (bhi * n + i) * d;
+        const T* kb = kT + bhi * (int64_t)d * m;
+        for (int t = lane; t < b; t += 32) {
+            T acc = T(0.f);
+            for (int cc = t; cc < d; cc += b) {
+                T diff = Ar::sub(qr[cc], kb[(int64_t)cc * m + j]);
+                acc = Ar::add(acc, Ar::nonneg(diff) ? diff : Ar::neg(diff));
+            }
+            sp[t] = acc;
+        }
+        __syncwarp();
+        for (int stride = b / 2; stride > 0; stride >>= 1) {
+            for (int t = lane; t < stride; t += 32) sp[t] = Ar::add(sp[t], sp[t + stride]);
+            __syncwarp();
+        }
+        if (lane == 0) s[o] = sp[0];
+        __syncwarp();
+    }
+}
+
+int check_args(const void* a, const void* b, const void* c, int64_t bh, int64_t n, int64_t m,
+               int64_t d, int dtype) {
+    if (dtype_size(dtype) == 0) { set_error("unsupported dtype code %d", dtype); return LF_ERR_DTYPE; }
+    if (bh < 0 || n < 0 || m < 0 || d < 0) { set_error("negative size"); return LF_ERR_INVALID; }
+    if (n > 0x7fffffffLL || m > 0x7fffffffLL || d > 0x7fffffffLL) {
+        set_error("sizes must fit in 31 bits per dimension"); return LF_ERR_UNSUPPORTED;
+    }
+    if ((bh > 0 && n > 0 && m > 0 && d > 0) && (!a || !b || !c)) { set_error("null pointer"); return LF_ERR_INVALID; }
+    return LF_OK;
+}
+
+}  // namespace
+}  // namespace lfb
+
+using namespace lfb;
+
+extern "C" int lf_laplace_sub_fwd(const void* q, const void* kT, void* s, int64_t bh, int64_t n,
+                                  int64_t m, int64_t d, int dtype, lf_stream_t stream) {
+    clear_error();
+    int rc = check_args(q, kT, s, bh, n, m, d, dtype);
+    if (rc) return rc;
+    if (bh == 0 || n == 0 || m == 0) return LF_OK;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (d == 0) {
+        if (cudaMemsetAsync(s, 0, (size_t)(bh * n * m) * dtype_size(dtype), st) != cudaSuccess)
+            return check_launch("memset");
+        return LF_OK;
+    }
+    LF_DISPATCH(dtype, T, return launch_fwd<T>(q, kT, s, bh, n, m, d, st));
+    return LF_OK;
+}
+
+static int bwd_common(const void* g, const void* q, const void* kT, void* dq, void* dk, int64_t bh,
+                      int64_t n, int64_t m, int64_t d, int dtype, lf_stream_t stream) {
+    int rc = check_args(g, q, kT, bh, n, m, d, dtype);
+    if (rc) return rc;
+    if (!dq && !dk) return LF_OK;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (bh == 0 || d == 0) return LF_OK;
+    if (n == 0 || m == 0) {  // empty reductions: gradients are zero
+        size_t es = dtype_size(dtype);
+        if (dq && cudaMemsetAsync(dq, 0, (size_t)(bh * n * d) * es, st) != cudaSuccess) return check_launch("memset");
+        if (dk && cudaMemsetAsync(dk, 0, (size_t)(bh * d * m) * es, st) != cudaSuccess) return check_launch("memset");
+        return LF_OK;
+    }
+    if (dq && dk) { LF_DISPATCH(dtype, T, return launch_bwd_t<T, true, true>(g, q, kT, dq, dk, bh, n, m, d, st)); }
+    if (dq) { LF_DISPATCH(dtype, T, return launch_bwd_t<T, true, false>(g, q, kT, dq, dk, bh, n, m, d, st)); }
+    LF_DISPATCH(dtype, T, return launch_bwd_t<T, false, true>(g, q, kT, dq, dk, bh, n, m, d, st));
+    return LF_OK;
+}
+
+extern "C" int lf_laplace_sub_bwd(const void* g, const void* q, const void* kT, void* dq, void* dkT,
+                                  int64_t bh, int64_t n, int64_t m, int64_t d, int dtype,
+                                  lf_stream_t stream) {
+    clear_error();
+    return bwd_common(g, q, kT, dq, dkT, bh, n, m, d, dtype, stream);
+}
+
+extern "C" int lf_laplace_sub_bwd_query(const void* g, const void* q, const void* kT, void* dq,
+                                        int64_t bh, int64_t n, int64_t m, int64_t d, int dtype,
+                                        lf_stream_t stream) {
+    clear_error();
+    if (!dq && bh * n * d > 0) { set_error("null gradQuery"); return LF_ERR_INVALID; }
+    return bwd_common(g, q, kT, dq, nullptr, bh, n, m, d, dtype, stream);
+}
+
+extern "C" int lf_laplace_sub_bwd_key(const void* g, const void* q, const void* kT, void* dkT,
+                                      int64_t bh, int64_t n, int64_t m, int64_t d, int dtype,
+                                      lf_stream_t stream) {
+    clear_error();
+    if (!dkT && bh * d * m > 0) { set_error("null gradKey"); return LF_ERR_INVALID; }
+    return bwd_common(g, q, kT, nullptr, dkT, bh, n, m, d, dtype, stream);
+}
+
+extern "C" int lf_laplace_sub_reduce_fwd(const void* q, const void* kT, void* s, int64_t bh,
+                                         int64_t n, int64_t m, int64_t d, int dtype,
+                                         lf_stream_t stream) {
+    clear_error();
+    int rc = check_args(q, kT, s, bh, n, m, d, dtype);
+    if (rc) return rc;
+    int64_t total = bh * n * m;
+    if (total == 0) return LF_OK;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (d == 0) {
+        if (cudaMemsetAsync(s, 0, (size_t)total * dtype_size(dtype), st) != cudaSuccess) return check_launch("memset");
+        return LF_OK;
+    }
+    int64_t warps_per_block = kThreads / 32;
+    int64_t blocks = (total + warps_per_block - 1) / warps_per_block;
+    int64_t cap = (int64_t)num_sms() * 16;
+    if (blocks > cap) blocks = cap;
+    LF_DISPATCH(dtype, T, {
+        lsub_reduce_kernel<T><<<(unsigned)blocks, kThreads, 0, st>>>(
+            static_cast<const T*>(q), static_cast<const T*>(kT), static_cast<T*>(s), total, (int)n,
+            (int)m, (int)d);
+        return check_launch("lsub_reduce_kernel");
+    });
+    return LF_OK;
+}

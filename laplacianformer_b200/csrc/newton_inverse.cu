@@ -1,0 +1,803 @@
+// NewtonInverse on B200 (sm_100a): batched Newton–Schulz inverse of small
+// square matrices and its analytic backward.
+//
+// Semantics follow src/NewtonInverse_cuda_kernel.cu of the reference:
+//   P = A + reg*I (reg = 0.01, :169), alpha = 1.8 / (max_i sum_j P_ij)^2
+//   (:82-120), V0 = alpha*P (:176-178), then `iters` times V <- 2V - V P V
+//   (:181-248 / :381-457); backward dA = -(V^T G V^T) (:469-573).
+// An extended initialisation X0 = P^T / (||P||_1 ||P||_inf) is also offered.
+//
+// Tensor-core path (fp32 / fp16 / bf16 inputs, n <= 128), one CTA per matrix:
+// * The matrix is zero padded to 128x128.  Every product runs on tcgen05 as
+//   kind::f16 MMAs (M = N = 128, K = 16) with fp32 accumulation in tensor
+//   memory.  Each fp32 operand X is split as X*s = hi + lo with hi, lo fp16
+//   and s a power of two that puts max|X*s| in [2^14, 2^15); the product is
+//   hi_a*hi_b + hi_a*lo_b + lo_a*hi_b (the lo*lo term is below 2^-22 of the
+//   result), i.e. about 22 significant bits — the same accuracy class as the
+//   reference's fp32 CUDA-core loops at twice the rate of a 3xTF32 split and
+//   with half its shared-memory footprint.
+// * P, V and W = V P are kept in shared memory as hi/lo fp16 in the 128-byte
+//   swizzled row-major layout; the same bytes serve as a K-major A operand
+//   and as an MN-major B operand, so no transposed copies are needed:
+//       W = V P  (A = V, B = P),   Y = W V  (A = W, B = V),   V <- 2V - Y.
+//   This is the association of the reference's 2-buffer kernel (:389-456).
+// * The exact fp32 V lives in tensor memory next to the accumulator (256
+//   columns in total), so the update 2V - Y is done in fp32.
+// * One elected thread issues the MMAs and commits them to an mbarrier; all
+//   waits are bounded and report LF_ERR_TIMEOUT through a device status word
+//   instead of hanging.
+//
+// CUDA-core path: fp64 inputs, the LF_NS_PREC_FP32_SIMT mode, the backward
+// and the residual use row-blocked fp32/fp64 FMA loops with V resident in
+// shared memory.
+#include "lf_common.cuh"
+
+namespace lfb {
+
+// Device status word: 0 = ok, otherwise an lf_status code set by a kernel
+// whose bounded wait expired.  Read and cleared by lf_device_status().
+__device__ int g_ns_status = 0;
+
+namespace {
+
+constexpr int kNsThreads = 256;
+constexpr int kTile = 128;                 // padded matrix size
+constexpr int kOpBytes = kTile * kTile * 2; // one fp16 operand (32 KB)
+constexpr int kTmemCols = 256;             // accumulator + fp32 V
+
+// ---------------------------------------------------------------------------
+// PTX wrappers (tcgen05, mbarrier, fences)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+// Returns true when the phase with the given parity has completed, false if
+// the bounded wait expired.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+    const uint32_t addr = smem_u32(bar);
+    for (uint32_t spin = 0; spin < (1u << 26); ++spin) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}\n"
+            : "=r"(done)
+            : "r"(addr), "r"(parity)
+            : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)), "r"(ncols) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// D[tmem] (+)= A[smem] * B[smem], kind::f16, cta_group::1.
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// 32 lanes x 32 consecutive 32-bit columns: thread i of the warp gets lane
+// (quadrant*32 + i), columns [col, col+32).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t* r = reinterpret_cast<uint32_t*>(v);
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+    const uint32_t* r = reinterpret_cast<const uint32_t*>(v);
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),
+        "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]),
+        "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// Ties registers written by tcgen05.ld to a point after tcgen05.wait::ld so
+// that the compiler cannot hoist their uses above the wait.
+__device__ __forceinline__ void reg_fence(float (&v)[32]) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) asm volatile("" : "+f"(v[i]));
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// ---------------------------------------------------------------------------
+// Operand layout: a 128x128 fp16 matrix X[r][c], row-major with the 128-byte
+// swizzle.  Columns [0,64) and [64,128) form two 16 KB blocks; row r of a
+// block is 128 bytes at r*128 and its 16-byte chunk k sits at chunk k^(r%8).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t op_chunk_offset(int r, int col8) {
+    // byte offset of the 16-byte chunk holding columns [8*col8, 8*col8+8) of row r
+    return (uint32_t)((col8 >> 3) * 16384 + r * 128 + (((col8 & 7) ^ (r & 7)) << 4));
+}
+
+// Shared-memory matrix descriptor (sm_100): start>>4 [0,14), LBO>>4 [16,30),
+// SBO>>4 [32,46), version 1 at bit 46, layout SWIZZLE_128B (2) at [61,64).
+__device__ __forceinline__ uint64_t make_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+    d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
+    d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)2 << 61;
+    return d;
+}
+// A operand (K-major view of the row-major layout), K step ks of 16 columns.
+__device__ __forceinline__ uint64_t desc_a(uint32_t base, int ks) {
+    return make_desc(base + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024);
+}
+// B operand (MN-major view: rows = k, contiguous columns = n), K step ks.
+__device__ __forceinline__ uint64_t desc_b(uint32_t base, int ks) {
+    return make_desc(base + ks * 2048, 16384, 1024);
+}
+// Instruction descriptor: D f32, A/B f16, A K-major, B MN-major, N = 128, M = 128.
+constexpr uint32_t kIdesc = (1u << 4) | (0u << 7) | (0u << 10) | (0u << 15) | (1u << 16) |
+                            ((uint32_t)(kTile >> 3) << 17) | ((uint32_t)(kTile >> 4) << 24);
+
+// Power-of-two scale that maps max|x| into [2^14, 2^15); 1 for 0 or non-finite.
+__device__ __forceinline__ float split_scale(float mx) {
+    if (!(mx > 0.f) || !isfinite(mx)) return 1.f;
+    int e;
+    frexpf(mx, &e);  // mx = f * 2^e, f in [0.5, 1)
+    return ldexpf(1.f, 15 - e);
+}
+
+__device__ __forceinline__ void split_store(unsigned char* hi_base, unsigned char* lo_base, int r,
+                                            int col0, const float (&v)[32], float s) {
+    // v holds columns [col0, col0+32) of row r; col0 is a multiple of 32.
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        uint32_t h[4], l[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            float x0 = v[8 * k + 2 * e] * s, x1 = v[8 * k + 2 * e + 1] * s;
+            __half h0 = __float2half_rn(x0), h1 = __float2half_rn(x1);
+            __half l0 = __float2half_rn(x0 - __half2float(h0));
+            __half l1 = __float2half_rn(x1 - __half2float(h1));
+            h[e] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+            l[e] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
+        }
+        uint32_t off = op_chunk_offset(r, (col0 >> 3) + k);
+        *reinterpret_cast<uint4*>(hi_base + off) = make_uint4(h[0], h[1], h[2], h[3]);
+        *reinterpret_cast<uint4*>(lo_base + off) = make_uint4(l[0], l[1], l[2], l[3]);
+    }
+}
+
+struct NsShared {
+    uint64_t bar;
+    uint32_t tmem_base;
+    int abort;
+    float red[kNsThreads / 32];
+    float colsum[kTile];
+    float scal[8];
+};
+
+// Issue one 128x128x128 product into the accumulator: nterm = 1 (hi*hi) or
+// 3 (hi*hi + hi*lo + lo*hi).
+__device__ __forceinline__ void issue_gemm(uint32_t acc, uint32_t a_hi, uint32_t a_lo, uint32_t b_hi,
+                                           uint32_t b_lo, int nterm) {
+#pragma unroll
+    for (int ks = 0; ks < kTile / 16; ++ks) {
+        mma_f16(acc, desc_a(a_hi, ks), desc_b(b_hi, ks), kIdesc, ks > 0 ? 1u : 0u);
+        if (nterm == 3) {
+            mma_f16(acc, desc_a(a_hi, ks), desc_b(b_lo, ks), kIdesc, 1u);
+            mma_f16(acc, desc_a(a_lo, ks), desc_b(b_hi, ks), kIdesc, 1u);
+        }
+    }
+}
+
+__device__ __forceinline__ float block_max(float v, NsShared& sh) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    const int warp = threadIdx.x >> 5;
+    __syncthreads();  // previous users of sh.red are done
+    if ((threadIdx.x & 31) == 0) sh.red[warp] = v;
+    __syncthreads();
+    float m = sh.red[0];
+#pragma unroll
+    for (int w = 1; w < kNsThreads / 32; ++w) m = fmaxf(m, sh.red[w]);
+    return m;
+}
+
+// grid = batch, block = 256 threads (8 warps).  Warp w owns TMEM lanes
+// 32*(w%4).. (matrix rows) and columns 64*(w/4).. of the 128x128 tile.
+template <typename T>
+__global__ void __launch_bounds__(kNsThreads, 1)
+ns_tc_fwd_kernel(const T* __restrict__ a, T* __restrict__ x, int n, int iters, int mode, float reg,
+                 int precision) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    unsigned char* Ph = base;
+    unsigned char* Pl = base + 1 * kOpBytes;
+    unsigned char* Vh = base + 2 * kOpBytes;
+    unsigned char* Vl = base + 3 * kOpBytes;
+    unsigned char* Wh = base + 4 * kOpBytes;
+    unsigned char* Wl = base + 5 * kOpBytes;
+    float* stage = reinterpret_cast<float*>(Wh);  // 128x128 fp32 during set-up (spans Wh and Wl)
+    NsShared& sh = *reinterpret_cast<NsShared*>(base + 6 * kOpBytes);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int quad = warp & 3, half = warp >> 2;
+    const int row = quad * 32 + lane;  // the matrix row this thread owns in the epilogues
+    const int64_t mat = blockIdx.x;
+    const T* A = a + mat * (int64_t)n * n;
+    T* X = x + mat * (int64_t)n * n;
+
+    if (tid == 0) {
+        mbar_init(&sh.bar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        sh.abort = 0;
+    }
+    if (tid < kTile) sh.colsum[tid] = 0.f;
+    if (warp == 0) tmem_alloc(&sh.tmem_base, kTmemCols);
+    __syncthreads();
+
+    // ---- set-up: P = A + reg I into the staging tile (swizzled fp32) -------
+    // Warp w loads rows w, w+8, ...; lane l holds columns 4l..4l+3.  Row sums
+    // (signed for alpha, absolute for ||P||_inf) by shuffles, column sums by
+    // per-lane accumulation.
+    float rowsum_max = -1e30f, rowabs_max = 0.f, pmax = 0.f;
+    float colacc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int i = warp; i < kTile; i += kNsThreads / 32) {
+        float v[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            int c = 4 * lane + e;
+            float t = 0.f;
+            if (i < n && c < n) t = Elem<T>::load(A[(int64_t)i * n + c]) + (i == c ? reg : 0.f);
+            v[e] = t;
+            stage[i * kTile + (c ^ (i & 31))] = t;
+            colacc[e] += fabsf(t);
+            pmax = fmaxf(pmax, fabsf(t));
+        }
+        float rs = 0.f, ra = 0.f;
+        if (mode == LF_NS_INIT_REFERENCE) {
+            // sequential sum like compute_alpha (:92-98) is not needed for a
+            // max; any order of the 128 padded terms is used here.
+            rs = (v[0] + v[1]) + (v[2] + v[3]);
+        }
+        ra = (fabsf(v[0]) + fabsf(v[1])) + (fabsf(v[2]) + fabsf(v[3]));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            rs += __shfl_xor_sync(0xffffffffu, rs, o);
+            ra += __shfl_xor_sync(0xffffffffu, ra, o);
+        }
+        if (i < n) {
+            rowsum_max = fmaxf(rowsum_max, rs);
+            rowabs_max = fmaxf(rowabs_max, ra);
+        }
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) atomicAdd(&sh.colsum[4 * lane + e], colacc[e]);
+    // Reduce the three maxima.
+    const float g_rowsum = block_max(rowsum_max, sh);
+    const float g_rowabs = block_max(rowabs_max, sh);
+    const float g_pmax = block_max(pmax, sh);
+    float colmax = (tid < kTile) ? sh.colsum[tid] : 0.f;
+    const float g_colabs = block_max(colmax, sh);
+
+    float v0_scale;  // V0 = v0_scale * P (or P^T)
+    if (mode == LF_NS_INIT_REFERENCE) {
+        v0_scale = __fdiv_rn(1.8f, g_rowsum * g_rowsum);
+    } else {
+        v0_scale = __fdiv_rn(1.0f, g_colabs * g_rowabs);
+    }
+    const float sP = split_scale(g_pmax);
+    float sV = split_scale(g_pmax * fabsf(v0_scale));
+
+    // Each thread converts its row segment: P -> (Ph, Pl), V0 -> (Vh, Vl) and
+    // the fp32 V0 -> TMEM columns [128, 256).
+    tc_fence_after();
+    const uint32_t tmem = sh.tmem_base;
+    const uint32_t t_lane = (uint32_t)(quad * 32) << 16;
+    const uint32_t t_acc = tmem + t_lane;            // accumulator columns [0,128)
+    const uint32_t t_v = tmem + t_lane + kTile;      // fp32 V columns [128,256)
+    for (int cb = 0; cb < 2; ++cb) {
+        const int col0 = half * 64 + cb * 32;
+        float pv[32], vv[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+            int c = col0 + e;
+            pv[e] = stage[row * kTile + (c ^ (row & 31))];
+            float src = (mode == LF_NS_INIT_REFERENCE) ? pv[e] : stage[c * kTile + (row ^ (c & 31))];
+            vv[e] = src * v0_scale;
+        }
+        split_store(Ph, Pl, row, col0, pv, sP);
+        if (iters > 0) split_store(Vh, Vl, row, col0, vv, sV);
+        tmem_st32(t_v + col0, vv);
+    }
+    tmem_wait_st();
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();  // staging reads done before W is overwritten; operands visible
+
+    const uint32_t aPh = smem_u32(Ph), aPl = smem_u32(Pl), aVh = smem_u32(Vh), aVl = smem_u32(Vl);
+    const uint32_t aWh = smem_u32(Wh), aWl = smem_u32(Wl);
+    uint32_t phase = 0;
+    bool ok = true;
+
+    for (int it = 0; it < iters && ok; ++it) {
+        const int nterm = (precision == LF_NS_PREC_MIXED && it < iters - 2) ? 1 : 3;
+        const bool last = (it == iters - 1);
+        // ---- W = V P ----------------------------------------------------
+        if (tid == 0) {
+            tc_fence_after();
+            issue_gemm(tmem, aVh, aVl, aPh, aPl, nterm);
+            mma_commit(&sh.bar);
+        }
+        ok = !__syncthreads_or(!mbar_wait(&sh.bar, phase));
+        phase ^= 1;
+        if (!ok) break;
+        tc_fence_after();
+        const float inv_v = 1.f / sV, inv_p = 1.f / sP;
+        float wv[2][32];
+        float wmax = 0.f;
+#pragma unroll
+        for (int cb = 0; cb < 2; ++cb) {
+            tmem_ld32(t_acc + half * 64 + cb * 32, wv[cb]);
+        }
+        tmem_wait_ld();
+        reg_fence(wv[0]);
+        reg_fence(wv[1]);
+#pragma unroll
+        for (int cb = 0; cb < 2; ++cb)
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+                wv[cb][e] = wv[cb][e] * inv_v * inv_p;
+                wmax = fmaxf(wmax, fabsf(wv[cb][e]));
+            }
+        const float sW = split_scale(block_max(wmax, sh));
+#pragma unroll
+        for (int cb = 0; cb < 2; ++cb) split_store(Wh, Wl, row, half * 64 + cb * 32, wv[cb], sW);
+        fence_async_smem();
+        tc_fence_before();
+        __syncthreads();
+        // ---- Y = W V ----------------------------------------------------
+        if (tid == 0) {
+            tc_fence_after();
+            issue_gemm(tmem, aWh, aWl, aVh, aVl, nterm);
+            mma_commit(&sh.bar);
+        }
+        ok = !__syncthreads_or(!mbar_wait(&sh.bar, phase));
+        phase ^= 1;
+        if (!ok) break;
+        tc_fence_after();
+        const float inv_w = 1.f / sW, inv_v2 = 1.f / sV;
+        float vmax = 0.f;
+#pragma unroll
+        for (int cb = 0; cb < 2; ++cb) {
+            float yv[32], vo[32];
+            tmem_ld32(t_acc + half * 64 + cb * 32, yv);
+            tmem_ld32(t_v + half * 64 + cb * 32, vo);
+            tmem_wait_ld();
+            reg_fence(yv);
+            reg_fence(vo);
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+                float vn = fmaf(2.f, vo[e], -(yv[e] * inv_w * inv_v2));
+                wv[cb][e] = vn;
+                vmax = fmaxf(vmax, fabsf(vn));
+            }
+            if (!last) tmem_st32(t_v + half * 64 + cb * 32, wv[cb]);
+        }
+        if (!last) {
+            tmem_wait_st();
+            sV = split_scale(block_max(vmax, sh));
+#pragma unroll
+            for (int cb = 0; cb < 2; ++cb) split_store(Vh, Vl, row, half * 64 + cb * 32, wv[cb], sV);
+            fence_async_smem();
+            tc_fence_before();
+            __syncthreads();
+        } else {
+            // Final iterate straight to global memory.
+            if (row < n) {
+#pragma unroll
+                for (int cb = 0; cb < 2; ++cb)
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) {
+                        int c = half * 64 + cb * 32 + e;
+                        if (c < n) X[(int64_t)row * n + c] = Elem<T>::store(wv[cb][e]);
+                    }
+            }
+        }
+    }
+    if (iters <= 0) {
+        // No iteration: the output is V0.
+        if (row < n) {
+            for (int cb = 0; cb < 2; ++cb) {
+                float vv[32];
+                tmem_ld32(t_v + half * 64 + cb * 32, vv);
+                tmem_wait_ld();
+                reg_fence(vv);
+#pragma unroll
+                for (int e = 0; e < 32; ++e) {
+                    int c = half * 64 + cb * 32 + e;
+                    if (c < n) X[(int64_t)row * n + c] = Elem<T>::store(vv[e]);
+                }
+            }
+        } else {
+            for (int cb = 0; cb < 2; ++cb) {
+                float vv[32];
+                tmem_ld32(t_v + half * 64 + cb * 32, vv);
+                tmem_wait_ld();
+            }
+        }
+    }
+    if (!ok && tid == 0) atomicExch(&g_ns_status, (int)LF_ERR_TIMEOUT);
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// CUDA-core kernels
+// ---------------------------------------------------------------------------
+constexpr int kRB = 16;  // rows per block in the row-blocked products
+
+// Block-wide reductions used in set-up.
+template <typename Acc>
+__device__ Acc block_reduce_max(Acc v, Acc* red) {
+    for (int o = 16; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    Acc m = red[0];
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) m = max(m, red[w]);
+    return m;
+}
+
+// V resident in shared memory as Acc [n][n+1]; the new iterate goes to a
+// second shared buffer, or to the output (type T == Acc) when two buffers do
+// not fit.  W = V P (P read from A on the fly) and Y = W V are formed 16 rows
+// at a time: the reference's (V P) V association.
+template <typename T, typename Acc, bool NEWV_GLOBAL>
+__global__ void __launch_bounds__(256)
+ns_simt_fwd_kernel(const T* __restrict__ a, T* __restrict__ x, int n, int iters, int mode, Acc reg) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int S = n + 1;
+    Acc* V = reinterpret_cast<Acc*>(smem_raw);
+    Acc* Vn = V + (size_t)n * S;                      // only when !NEWV_GLOBAL
+    Acc* Wr = Vn + (NEWV_GLOBAL ? 0 : (size_t)n * S); // kRB x S
+    Acc* red = Wr + kRB * S;                          // 8 entries
+    const int tid = threadIdx.x;
+    const int64_t mat = blockIdx.x;
+    const T* A = a + mat * (int64_t)n * n;
+    T* X = x + mat * (int64_t)n * n;
+    auto P = [&](int i, int j) -> Acc { return (Acc)Elem<T>::load(A[(int64_t)i * n + j]) + (i == j ? reg : Acc(0)); };
+
+    // Initialisation.
+    Acc c0;
+    if (mode == LF_NS_INIT_REFERENCE) {
+        Acc mx = Acc(-1e30);
+        for (int i = tid; i < n; i += blockDim.x) {
+            Acc s = 0;
+            for (int j = 0; j < n; ++j) s += P(i, j);
+            mx = max(mx, s);
+        }
+        mx = block_reduce_max<Acc>(mx, red);
+        c0 = Acc(1.8) / (mx * mx);
+    } else {
+        Acc r1 = 0, ri = 0;
+        for (int i = tid; i < n; i += blockDim.x) {
+            Acc rs = 0, cs = 0;
+            for (int j = 0; j < n; ++j) { rs += fabs(P(i, j)); cs += fabs(P(j, i)); }
+            ri = max(ri, rs);
+            r1 = max(r1, cs);
+        }
+        ri = block_reduce_max<Acc>(ri, red);
+        r1 = block_reduce_max<Acc>(r1, red);
+        c0 = Acc(1) / (r1 * ri);
+    }
+    for (int e = tid; e < n * n; e += blockDim.x) {
+        int i = e / n, j = e - i * n;
+        V[i * S + j] = (mode == LF_NS_INIT_REFERENCE ? P(i, j) : P(j, i)) * c0;
+    }
+    __syncthreads();
+
+    const int tpr = blockDim.x / kRB;  // threads per row of the block (16)
+    const int rr = tid / tpr, tj = tid - rr * tpr;
+    for (int it = 0; it < iters; ++it) {
+        for (int r0 = 0; r0 < n; r0 += kRB) {
+            const int r = r0 + rr;
+            // W[rr][j] = sum_k V[r][k] P[k][j]
+            for (int j = tj; j < n; j += tpr) {
+                Acc acc = 0;
+                if (r < n)
+                    for (int k = 0; k < n; ++k) acc = fma(V[r * S + k], P(k, j), acc);
+                Wr[rr * S + j] = acc;
+            }
+            __syncthreads();
+            // Y[r][j] = sum_k W[rr][k] V[k][j];  V'[r][j] = 2 V[r][j] - Y
+            if (r < n) {
+                for (int j = tj; j < n; j += tpr) {
+                    Acc acc = 0;
+                    for (int k = 0; k < n; ++k) acc = fma(Wr[rr * S + k], V[k * S + j], acc);
+                    Acc vn = fma(Acc(2), V[r * S + j], -acc);
+                    if (NEWV_GLOBAL) X[(int64_t)r * n + j] = (T)vn;
+                    else Vn[r * S + j] = vn;
+                }
+            }
+            __syncthreads();
+        }
+        if (NEWV_GLOBAL) {
+            __threadfence_block();
+            for (int e = tid; e < n * n; e += blockDim.x) {
+                int i = e / n, j = e - i * n;
+                V[i * S + j] = (Acc)X[e];
+            }
+        } else {
+            for (int e = tid; e < n * n; e += blockDim.x) {
+                int i = e / n, j = e - i * n;
+                V[i * S + j] = Vn[i * S + j];
+            }
+        }
+        __syncthreads();
+    }
+    for (int e = tid; e < n * n; e += blockDim.x) {
+        int i = e / n, j = e - i * n;
+        X[e] = Elem<T>::store(V[i * S + j]);
+    }
+}
+
+// dA = -(V^T G) V^T, V resident in shared memory, G read from global.
+template <typename T, typename Acc>
+__global__ void __launch_bounds__(256)
+ns_simt_bwd_kernel(const T* __restrict__ g, const T* __restrict__ v, T* __restrict__ da, int n) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int S = n + 1;
+    Acc* V = reinterpret_cast<Acc*>(smem_raw);
+    Acc* Tr = V + (size_t)n * S;
+    const int tid = threadIdx.x;
+    const int64_t mat = blockIdx.x;
+    const T* G = g + mat * (int64_t)n * n;
+    const T* Vg = v + mat * (int64_t)n * n;
+    T* O = da + mat * (int64_t)n * n;
+    for (int e = tid; e < n * n; e += blockDim.x) {
+        int i = e / n, j = e - i * n;
+        V[i * S + j] = (Acc)Elem<T>::load(Vg[e]);
+    }
+    __syncthreads();
+    const int tpr = blockDim.x / kRB;
+    const int rr = tid / tpr, tj = tid - rr * tpr;
+    for (int r0 = 0; r0 < n; r0 += kRB) {
+        const int r = r0 + rr;
+        for (int j = tj; j < n; j += tpr) {
+            Acc acc = 0;
+            if (r < n)
+                for (int p = 0; p < n; ++p) acc = fma(V[p * S + r], (Acc)Elem<T>::load(G[(int64_t)p * n + j]), acc);
+            Tr[rr * S + j] = acc;
+        }
+        __syncthreads();
+        if (r < n) {
+            for (int j = tj; j < n; j += tpr) {
+                Acc acc = 0;
+                for (int k = 0; k < n; ++k) acc = fma(Tr[rr * S + k], V[j * S + k], acc);
+                O[(int64_t)r * n + j] = Elem<T>::store(-acc);
+            }
+        }
+        __syncthreads();
+    }
+}
+
+// res[b] = ||(A + reg I) X - I||_F, accumulated in Acc.
+template <typename T, typename Acc>
+__global__ void __launch_bounds__(256)
+ns_residual_kernel(const T* __restrict__ a, const T* __restrict__ x, Acc* __restrict__ res, int n, Acc reg) {
+    __shared__ Acc red[8];
+    const int64_t mat = blockIdx.x;
+    const T* A = a + mat * (int64_t)n * n;
+    const T* X = x + mat * (int64_t)n * n;
+    Acc ss = 0;
+    for (int e = threadIdx.x; e < n * n; e += blockDim.x) {
+        int i = e / n, j = e - i * n;
+        Acc acc = 0;
+        for (int k = 0; k < n; ++k)
+            acc = fma((Acc)Elem<T>::load(A[(int64_t)i * n + k]) + (i == k ? reg : Acc(0)),
+                      (Acc)Elem<T>::load(X[(int64_t)k * n + j]), acc);
+        acc -= (i == j) ? Acc(1) : Acc(0);
+        ss = fma(acc, acc, ss);
+    }
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        Acc t = 0;
+        for (int w = 0; w < 8; ++w) t += red[w];
+        res[mat] = sqrt(t);
+    }
+}
+
+size_t tc_smem_bytes() { return 6 * (size_t)kOpBytes + sizeof(NsShared) + 1024; }
+
+template <typename T>
+int launch_tc_fwd(const void* a, void* x, int64_t batch, int64_t n, int iters, int mode, float reg,
+                  int precision, cudaStream_t st) {
+    size_t smem = tc_smem_bytes();
+    if (smem > (size_t)max_optin_smem()) {
+        set_error("NewtonInverse tensor-core path needs %zu bytes of shared memory", smem);
+        return LF_ERR_UNSUPPORTED;
+    }
+    auto kern = ns_tc_fwd_kernel<T>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    kern<<<(unsigned)batch, kNsThreads, smem, st>>>(static_cast<const T*>(a), static_cast<T*>(x), (int)n, iters,
+                                                    mode, reg, precision);
+    return check_launch("ns_tc_fwd_kernel");
+}
+
+template <typename T>
+int launch_simt_fwd(const void* a, void* x, int64_t batch, int64_t n, int iters, int mode, double reg,
+                    cudaStream_t st) {
+    using Acc = typename Elem<T>::acc;
+    const size_t S = (size_t)n + 1;
+    size_t one = (size_t)n * S * sizeof(Acc);
+    size_t extra = (size_t)kRB * S * sizeof(Acc) + 8 * sizeof(Acc);
+    size_t smem2 = 2 * one + extra, smem1 = one + extra;
+    size_t cap = (size_t)max_optin_smem();
+    if (smem2 <= cap) {
+        auto kern = ns_simt_fwd_kernel<T, Acc, false>;
+        if (smem2 > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem2);
+        kern<<<(unsigned)batch, 256, smem2, st>>>(static_cast<const T*>(a), static_cast<T*>(x), (int)n, iters, mode, (Acc)reg);
+        return check_launch("ns_simt_fwd_kernel");
+    }
+    if constexpr (sizeof(T) == sizeof(Acc)) {
+        if (smem1 <= cap) {
+            auto kern = ns_simt_fwd_kernel<T, Acc, true>;
+            if (smem1 > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem1);
+            kern<<<(unsigned)batch, 256, smem1, st>>>(static_cast<const T*>(a), static_cast<T*>(x), (int)n, iters, mode, (Acc)reg);
+            return check_launch("ns_simt_fwd_kernel");
+        }
+    }
+    set_error("NewtonInverse: n=%lld does not fit in shared memory", (long long)n);
+    return LF_ERR_UNSUPPORTED;
+}
+
+template <typename T>
+int launch_simt_bwd(const void* g, const void* v, void* da, int64_t batch, int64_t n, cudaStream_t st) {
+    using Acc = typename Elem<T>::acc;
+    const size_t S = (size_t)n + 1;
+    size_t smem = ((size_t)n * S + (size_t)kRB * S) * sizeof(Acc);
+    if (smem > (size_t)max_optin_smem()) {
+        set_error("NewtonInverse backward: n=%lld does not fit in shared memory", (long long)n);
+        return LF_ERR_UNSUPPORTED;
+    }
+    auto kern = ns_simt_bwd_kernel<T, Acc>;
+    if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    kern<<<(unsigned)batch, 256, smem, st>>>(static_cast<const T*>(g), static_cast<const T*>(v), static_cast<T*>(da), (int)n);
+    return check_launch("ns_simt_bwd_kernel");
+}
+
+int check_ns(const void* a, const void* x, int64_t batch, int64_t n, int dtype) {
+    if (dtype_size(dtype) == 0) { set_error("unsupported dtype code %d", dtype); return LF_ERR_DTYPE; }
+    if (batch < 0 || n < 0) { set_error("negative size"); return LF_ERR_INVALID; }
+    if (batch > 0x7fffffffLL) { set_error("batch too large"); return LF_ERR_UNSUPPORTED; }
+    if (n > kTile) { set_error("NewtonInverse supports n <= %d (got %lld)", kTile, (long long)n); return LF_ERR_UNSUPPORTED; }
+    if (batch > 0 && n > 0 && (!a || !x)) { set_error("null pointer"); return LF_ERR_INVALID; }
+    return LF_OK;
+}
+
+}  // namespace
+}  // namespace lfb
+
+using namespace lfb;
+
+extern "C" int lf_newton_inverse_supported(int64_t n) { return (n >= 1 && n <= kTile) ? 1 : 0; }
+
+extern "C" int lf_newton_inverse_fwd_ex(const void* a, void* x, int64_t batch, int64_t n, int iters,
+                                        int dtype, int init_mode, double reg, int precision,
+                                        lf_stream_t stream) {
+    clear_error();
+    int rc = check_ns(a, x, batch, n, dtype);
+    if (rc) return rc;
+    if (init_mode != LF_NS_INIT_REFERENCE && init_mode != LF_NS_INIT_SCALED_TRANSPOSE) {
+        set_error("unknown init mode %d", init_mode);
+        return LF_ERR_INVALID;
+    }
+    if (precision < LF_NS_PREC_SPLIT3 || precision > LF_NS_PREC_FP32_SIMT) {
+        set_error("unknown precision %d", precision);
+        return LF_ERR_INVALID;
+    }
+    if (batch == 0 || n == 0) return LF_OK;
+    if (iters < 0) iters = 0;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (dtype == LF_F64) return launch_simt_fwd<double>(a, x, batch, n, iters, init_mode, reg, st);
+    if (precision == LF_NS_PREC_FP32_SIMT) {
+        LF_DISPATCH(dtype, T, return launch_simt_fwd<T>(a, x, batch, n, iters, init_mode, reg, st));
+    }
+    switch (dtype) {
+        case LF_F32: return launch_tc_fwd<float>(a, x, batch, n, iters, init_mode, (float)reg, precision, st);
+        case LF_F16: return launch_tc_fwd<__half>(a, x, batch, n, iters, init_mode, (float)reg, precision, st);
+        case LF_BF16: return launch_tc_fwd<__nv_bfloat16>(a, x, batch, n, iters, init_mode, (float)reg, precision, st);
+        default: break;
+    }
+    set_error("unsupported dtype code %d", dtype);
+    return LF_ERR_DTYPE;
+}
+
+extern "C" int lf_newton_inverse_fwd(const void* a, void* x, int64_t batch, int64_t n, int iters, int dtype,
+                                     lf_stream_t stream) {
+    return lf_newton_inverse_fwd_ex(a, x, batch, n, iters, dtype, LF_NS_INIT_REFERENCE, 0.01,
+                                    LF_NS_PREC_SPLIT3, stream);
+}
+
+extern "C" int lf_newton_inverse_bwd(const void* g, const void* v, void* da, int64_t batch, int64_t n, int dtype,
+                                     lf_stream_t stream) {
+    clear_error();
+    int rc = check_ns(g, v, batch, n, dtype);
+    if (rc) return rc;
+    if (!da && batch * n > 0) { set_error("null grad_mat"); return LF_ERR_INVALID; }
+    if (batch == 0 || n == 0) return LF_OK;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    LF_DISPATCH(dtype, T, return launch_simt_bwd<T>(g, v, da, batch, n, st));
+    return LF_OK;
+}
+
+extern "C" int lf_newton_inverse_residual(const void* a, const void* x, void* res, int64_t batch, int64_t n,
+                                          double reg, int dtype, lf_stream_t stream) {
+    clear_error();
+    int rc = check_ns(a, x, batch, n, dtype);
+    if (rc) return rc;
+    if (!res && batch > 0) { set_error("null residual output"); return LF_ERR_INVALID; }
+    if (batch == 0) return LF_OK;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (n == 0) {
+        if (cudaMemsetAsync(res, 0, (size_t)batch * (dtype == LF_F64 ? 8 : 4), st) != cudaSuccess) return check_launch("memset");
+        return LF_OK;
+    }
+    LF_DISPATCH(dtype, T, {
+        using Acc = typename Elem<T>::acc;
+        ns_residual_kernel<T, Acc><<<(unsigned)batch, 256, 0, st>>>(static_cast<const T*>(a), static_cast<const T*>(x),
+                                                                    static_cast<Acc*>(res), (int)n, (Acc)reg);
+        return check_launch("ns_residual_kernel");
+    });
+    return LF_OK;
+}
+
+// Synchronises the current device and returns (and optionally clears) the
+// status word set by kernels whose bounded waits expired.
+extern "C" int lf_device_status(int clear) {
+    clear_error();
+    if (cudaDeviceSynchronize() != cudaSuccess) return check_launch("cudaDeviceSynchronize");
+    int v = 0;
+    if (cudaMemcpyFromSymbol(&v, g_ns_status, sizeof(int)) != cudaSuccess) return check_launch("status read");
+    if (clear && v) {
+        int z = 0;
+        if (cudaMemcpyToSymbol(g_ns_status, &z, sizeof(int)) != cudaSuccess) return check_launch("status clear");
+    }
+    return v;
+}

@@ -1,0 +1,266 @@
+"""LaplaceSubtraction on the GPU, through the C ABI (liblfb200.so) and the
+drop-in extension, against the CPU oracle and — where it was built — the
+reference operators compiled for sm_100 (oracle/_ref)."""
+import numpy as np
+import pytest
+import torch
+
+from laplacianformer_b200 import capi
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [
+    # B, H, N, D, M
+    (2, 2, 70, 32, 49),      # configuration-2 shape, scaled down
+    (1, 3, 33, 17, 5),       # ragged channels / landmarks
+    (1, 1, 1, 1, 1),         # minimum
+    (1, 2, 600, 64, 64),     # d = 64, m = 64, several row tiles
+    (1, 1, 37, 48, 9),       # non power-of-two channels
+    (3, 1, 9, 100, 256),     # many landmarks, d > 64
+    (1, 1, 1500, 8, 196),    # m = 196 (landmark-vs-key shape)
+]
+
+
+def _inputs(shape, dtype, seed=0, device="cuda"):
+    B, H, N, D, M = shape
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(B, H, N, D, generator=g).to(dtype)
+    k = torch.randn(B, H, D, M, generator=g).to(dtype)
+    gr = torch.randn(B, H, N, M, generator=g).to(dtype)
+    return q, k, gr
+
+
+def _np(t):
+    return t.detach().cpu().to(torch.float64 if t.dtype == torch.float64 else torch.float32).numpy()
+
+
+@pytest.mark.parametrize("shape", SHAPES, ids=str)
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float64, torch.float16, torch.bfloat16], ids=str)
+def test_forward_bit_exact_vs_oracle(cuda, shape, dtype):
+    q, k, _ = _inputs(shape, dtype)
+    s = capi.laplace_sub_fwd(q.to(cuda), k.to(cuda))
+    torch.cuda.synchronize()
+    ref = O.laplace_fwd(q, k)
+    ref = ref.float().numpy() if isinstance(ref, torch.Tensor) else np.asarray(ref, dtype=np.float64)
+    # Sequential fp32 (fp64) sum over channels, same operations as the
+    # reference kernel, rounded once to the storage type: identical bits.
+    np.testing.assert_array_equal(_np(s).astype(np.float64), np.asarray(ref, dtype=np.float64))
+
+
+def _bwd_tol(dtype):
+    return {torch.float32: 1e-5, torch.float64: 1e-12, torch.float16: 1e-2, torch.bfloat16: 1e-2}[dtype]
+
+
+@pytest.mark.parametrize("shape", SHAPES, ids=str)
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float64, torch.float16, torch.bfloat16], ids=str)
+def test_backward_vs_oracle(cuda, shape, dtype):
+    q, k, g = _inputs(shape, dtype, seed=1)
+    dq, dk = capi.laplace_sub_bwd(g.to(cuda), q.to(cuda), k.to(cuda))
+    dq_only = capi.laplace_sub_bwd_query(g.to(cuda), q.to(cuda), k.to(cuda))
+    dk_only = capi.laplace_sub_bwd_key(g.to(cuda), q.to(cuda), k.to(cuda))
+    torch.cuda.synchronize()
+    rq = np.asarray(O.laplace_bwd_query(g.float() if dtype != torch.float64 else g, q.float() if dtype != torch.float64 else q, k.float() if dtype != torch.float64 else k), dtype=np.float64)
+    rk = np.asarray(O.laplace_bwd_key(g.float() if dtype != torch.float64 else g, q.float() if dtype != torch.float64 else q, k.float() if dtype != torch.float64 else k), dtype=np.float64)
+    ga = np.abs(_np(g).astype(np.float64))
+    tol = _bwd_tol(dtype)
+    # The reduction order differs from the reference, so the bound is
+    # relative to the sum of |terms|: sum_j |g| per row for dQ, sum_i |g|
+    # per landmark for dK.
+    row = ga.sum(-1, keepdims=True)
+    col = ga.sum(-2)[:, :, None, :]
+    for got in (dq, dq_only):
+        assert np.all(np.abs(_np(got) - rq) <= tol * row + 1e-30)
+    for got in (dk, dk_only):
+        assert np.all(np.abs(_np(got) - rk) <= tol * col + 1e-30)
+    # dQ-only / dK-only kernels agree with the fused one
+    np.testing.assert_allclose(_np(dq_only), _np(dq), rtol=0, atol=float(tol * row.max()))
+    np.testing.assert_allclose(_np(dk_only), _np(dk), rtol=0, atol=float(tol * col.max()))
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16], ids=str)
+def test_backward_ties_give_zero_sign(cuda, dtype):
+    # Queries equal to landmark values (the LaplaceSub(L, L^T) case) must use
+    # sign(0) = 0 exactly.
+    g0 = torch.Generator().manual_seed(5)
+    L = torch.randn(2, 1, 24, 16, generator=g0).to(dtype)   # [B,H,M,D]
+    q = L.clone()
+    k = L.transpose(-1, -2).contiguous()
+    g = torch.randn(2, 1, 24, 24, generator=g0).to(dtype)
+    dq, dk = capi.laplace_sub_bwd(g.to(cuda), q.to(cuda), k.to(cuda))
+    s = capi.laplace_sub_fwd(q.to(cuda), k.to(cuda))
+    torch.cuda.synchronize()
+    assert torch.all(torch.diagonal(s.float().cpu(), dim1=-2, dim2=-1) == 0)
+    rq = O.laplace_bwd_query(g.float(), q.float(), k.float())
+    rk = O.laplace_bwd_key(g.float(), q.float(), k.float())
+    row = np.abs(_np(g)).sum(-1, keepdims=True)
+    col = np.abs(_np(g)).sum(-2)[:, :, None, :]
+    tol = _bwd_tol(dtype)
+    assert np.all(np.abs(_np(dq) - np.asarray(rq, np.float64)) <= tol * row)
+    assert np.all(np.abs(_np(dk) - np.asarray(rk, np.float64)) <= tol * col)
+
+
+@pytest.mark.parametrize("shape", [(1, 2, 20, 32, 7), (1, 1, 11, 48, 5), (2, 1, 5, 300, 3), (1, 1, 4, 24, 3)], ids=str)
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float64, torch.float16], ids=str)
+def test_reduce_forward_bit_exact_vs_oracle(cuda, shape, dtype):
+    q, k, _ = _inputs(shape, dtype, seed=2)
+    r = capi.laplace_sub_reduce_fwd(q.to(cuda), k.to(cuda))
+    torch.cuda.synchronize()
+    ref = O.laplace_reduce(q.numpy() if dtype != torch.float16 else q.numpy(), k.numpy())
+    got = r.cpu().numpy()
+    if dtype == torch.float16:
+        np.testing.assert_array_equal(got.view(np.uint16), np.asarray(ref).view(np.uint16))
+    else:
+        np.testing.assert_array_equal(got, ref)
+
+
+def test_empty_and_degenerate(cuda):
+    # empty batch / rows / landmarks: nothing to do, no error
+    for B, H, N, D, M in [(0, 2, 5, 4, 3), (1, 1, 0, 4, 3), (1, 1, 5, 4, 0)]:
+        q = torch.randn(B, H, N, D, device=cuda)
+        k = torch.randn(B, H, D, M, device=cuda)
+        g = torch.randn(B, H, N, M, device=cuda)
+        s = capi.laplace_sub_fwd(q, k)
+        dq, dk = capi.laplace_sub_bwd(g, q, k)
+        assert s.shape == (B, H, N, M)
+        if N == 0 and B * H > 0:
+            assert torch.all(dk == 0)
+    # d = 0: distances are 0
+    q = torch.randn(1, 1, 5, 0, device=cuda)
+    k = torch.randn(1, 1, 0, 3, device=cuda)
+    s = capi.laplace_sub_fwd(q, k)
+    assert torch.all(s == 0)
+
+
+def test_large_offsets_64bit(cuda):
+    # bh*n*m beyond 2^31 elements would overflow the reference's int offsets
+    # (LaplaceSubtraction_cuda_kernel.cu:70-72); here the last (b,h) slice of
+    # a 2^31+ element output is checked.  bh = 2, n = 2^20 + 1, m = 1024.
+    bh, n, d, m = 2, (1 << 20) + 1, 4, 1024
+    q = torch.randn(1, bh, n, d, device=cuda)
+    k = torch.randn(1, bh, d, m, device=cuda)
+    s = capi.laplace_sub_fwd(q, k)
+    torch.cuda.synchronize()
+    tail_q = q[:, 1:, -3:].cpu()
+    ref = O.laplace_fwd(tail_q.numpy(), k[:, 1:].cpu().numpy())
+    np.testing.assert_array_equal(s[:, 1:, -3:].cpu().numpy(), ref)
+    del s
+
+
+def test_canary_padding_untouched(cuda):
+    # Outputs written through a view into a larger buffer must not spill.
+    B, H, N, D, M = 1, 2, 45, 19, 13
+    q, k, g = _inputs((B, H, N, D, M), torch.float32, seed=3)
+    q, k, g = q.to(cuda), k.to(cuda), g.to(cuda)
+    buf = torch.full((B * H * N * M + 64,), 12345.0, device=cuda)
+    out = buf[32:32 + B * H * N * M].view(B, H, N, M)
+    capi.laplace_sub_fwd(q, k, out)
+    dqbuf = torch.full((B * H * N * D + 64,), 777.0, device=cuda)
+    dkbuf = torch.full((B * H * D * M + 64,), 777.0, device=cuda)
+    capi.laplace_sub_bwd(g, q, k, dqbuf[32:32 + B * H * N * D].view(B, H, N, D), dkbuf[32:32 + B * H * D * M].view(B, H, D, M))
+    torch.cuda.synchronize()
+    assert torch.all(buf[:32] == 12345.0) and torch.all(buf[-32:] == 12345.0)
+    assert torch.all(dqbuf[:32] == 777.0) and torch.all(dqbuf[-32:] == 777.0)
+    assert torch.all(dkbuf[:32] == 777.0) and torch.all(dkbuf[-32:] == 777.0)
+
+
+def test_config2_full_size_properties(cuda):
+    # Full configuration-2 size: bit-exact forward on sampled (b,h) slices,
+    # and backward consistency between the fused and single-output kernels.
+    from laplacianformer_b200 import workloads
+
+    w = workloads.config2(device=cuda)
+    q, kT, ds = w["q"], w["kT"], w["ds"]
+    s = capi.laplace_sub_fwd(q, kT)
+    dq, dk = capi.laplace_sub_bwd(ds, q, kT)
+    torch.cuda.synchronize()
+    for b, h in [(0, 0), (17, 1), (31, 1)]:
+        ref = O.laplace_fwd(q[b:b + 1, h:h + 1].cpu().numpy(), kT[b:b + 1, h:h + 1].cpu().numpy())
+        np.testing.assert_array_equal(s[b:b + 1, h:h + 1].cpu().numpy(), ref)
+        rq = O.laplace_bwd_query(ds[b:b + 1, h:h + 1].cpu().numpy(), q[b:b + 1, h:h + 1].cpu().numpy(), kT[b:b + 1, h:h + 1].cpu().numpy())
+        rk = O.laplace_bwd_key(ds[b:b + 1, h:h + 1].cpu().numpy(), q[b:b + 1, h:h + 1].cpu().numpy(), kT[b:b + 1, h:h + 1].cpu().numpy())
+        ga = np.abs(ds[b:b + 1, h:h + 1].cpu().numpy().astype(np.float64))
+        assert np.all(np.abs(dq[b:b + 1, h:h + 1].cpu().numpy() - rq) <= 1e-5 * ga.sum(-1, keepdims=True))
+        assert np.all(np.abs(dk[b:b + 1, h:h + 1].cpu().numpy() - rk) <= 1e-5 * ga.sum(-2)[:, :, None, :])
+
+
+def test_errors_are_reported(cuda):
+    q = torch.randn(1, 1, 4, 3, device=cuda)
+    k = torch.randn(1, 1, 3, 2, device=cuda)
+    with pytest.raises(capi.LfError) as e:
+        capi.lib()  # noqa: B018
+        rc = capi.lib().lf_laplace_sub_fwd(q.data_ptr(), k.data_ptr(), q.data_ptr(), 1, 4, 2, 3, 9, None)
+        capi._check(rc, "lf_laplace_sub_fwd")
+    assert e.value.code == capi.LF_ERR_DTYPE
+    rc = capi.lib().lf_laplace_sub_fwd(None, k.data_ptr(), q.data_ptr(), 1, 4, 2, 3, 0, None)
+    assert rc == capi.LF_ERR_INVALID
+
+
+# ---------------------------------------------------------------------------
+# The drop-in extension (reference names and out-parameter contract)
+# ---------------------------------------------------------------------------
+def test_extension_ops_match_capi(cuda, ext):
+    q, k, g = (t.to(cuda) for t in _inputs((2, 2, 70, 32, 49), torch.float32, seed=4))
+    s = torch.empty(2, 2, 70, 49, device=cuda)
+    ext.LaplaceSubtraction_forward(q, k, s)
+    dq = torch.full_like(q, float("nan"))
+    dk = torch.full_like(k, float("nan"))
+    ext.LaplaceSubtraction_backward_query(g, q, k, dq)
+    ext.LaplaceSubtraction_backward_key(g, q, k, dk)
+    r = torch.empty_like(s)
+    ext.LaplaceSubtraction_reduce_forward(q, k, r)
+    torch.cuda.synchronize()
+    assert torch.equal(s, capi.laplace_sub_fwd(q, k))
+    dq2, dk2 = capi.laplace_sub_bwd(g, q, k)
+    torch.testing.assert_close(dq, dq2, rtol=0, atol=1e-4)
+    torch.testing.assert_close(dk, dk2, rtol=0, atol=1e-4)
+    assert torch.equal(r, capi.laplace_sub_reduce_fwd(q, k))
+    with pytest.raises(RuntimeError, match="query and key must match"):
+        ext.LaplaceSubtraction_forward(q, k[:, :, :5].contiguous(), s)
+    with pytest.raises(RuntimeError, match="contiguous"):
+        ext.LaplaceSubtraction_forward(q.transpose(2, 3), k, s)
+
+
+def test_autograd_function(cuda):
+    from laplacianformer_b200.ops import laplace_subtraction
+
+    g0 = torch.Generator().manual_seed(9)
+    q = torch.randn(1, 2, 40, 8, generator=g0, dtype=torch.float64).to(cuda).requires_grad_()
+    k = torch.randn(1, 2, 8, 6, generator=g0, dtype=torch.float64).to(cuda).requires_grad_()
+    s = laplace_subtraction(q, k)
+    ref = (q.detach()[..., :, None, :] - k.detach().transpose(-1, -2)[..., None, :, :]).abs().sum(-1)
+    torch.testing.assert_close(s, ref)
+    up = torch.randn_like(s)
+    s.backward(up)
+    qq = q.detach().clone().requires_grad_()
+    kk = k.detach().clone().requires_grad_()
+    (qq[..., :, None, :] - kk.transpose(-1, -2)[..., None, :, :]).abs().sum(-1).backward(up)
+    torch.testing.assert_close(q.grad, qq.grad)
+    torch.testing.assert_close(k.grad, kk.grad)
+
+
+# ---------------------------------------------------------------------------
+# Against the reference operators themselves (oracle/_ref), when built
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.float64], ids=str)
+def test_against_reference_module(cuda, ref_module, dtype):
+    if ref_module is None:
+        pytest.skip("oracle/_ref not built (python oracle/build_ref.py)")
+    from laplacianformer_b200 import workloads
+
+    w = workloads.config2(device=cuda, dtype=dtype, batch=4)
+    q, kT, ds = w["q"], w["kT"], w["ds"]
+    s_ref = torch.empty(4, 2, 3136, 49, device=cuda, dtype=dtype)
+    ref_module.LaplaceSubtraction_forward(q, kT, s_ref)
+    s = capi.laplace_sub_fwd(q, kT)
+    dq_ref = torch.empty_like(q)
+    dk_ref = torch.empty_like(kT)
+    ref_module.LaplaceSubtraction_backward_query(ds, q, kT, dq_ref)
+    ref_module.LaplaceSubtraction_backward_key(ds, q, kT, dk_ref)
+    dq, dk = capi.laplace_sub_bwd(ds, q, kT)
+    torch.cuda.synchronize()
+    assert torch.equal(s, s_ref)
+    ga = ds.double().abs()
+    tol = _bwd_tol(dtype) if dtype != torch.float16 else 2e-2
+    assert torch.all((dq.double() - dq_ref.double()).abs() <= tol * ga.sum(-1, keepdim=True) + 1e-30)
+    assert torch.all((dk.double() - dk_ref.double()).abs() <= tol * ga.sum(-2).unsqueeze(-2) + 1e-30)

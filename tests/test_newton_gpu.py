@@ -1,0 +1,165 @@
+"""NewtonInverse on the GPU (tcgen05 split-fp16 path and CUDA-core path)
+against the CPU oracle and, where built, the reference operators."""
+import numpy as np
+import pytest
+import torch
+
+from laplacianformer_b200 import capi
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def spd(batch, n, seed, d=16, sigma=4.0, ridge=1e-3):
+    g = torch.Generator().manual_seed(seed)
+    L = torch.randn(batch, n, d, generator=g, dtype=torch.float64)
+    A = torch.exp(-torch.cdist(L, L, p=1) / sigma) + ridge * torch.eye(n, dtype=torch.float64)
+    return A.float().view(1, batch, n, n)
+
+
+def _res(A, X, reg):
+    return O.residual_fro(np.asarray(A, np.float64), np.asarray(X, np.float64), reg)
+
+
+@pytest.mark.parametrize("n", [1, 7, 16, 49, 64, 100, 127, 128])
+@pytest.mark.parametrize("mode", [capi.INIT_REFERENCE, capi.INIT_SCALED_TRANSPOSE])
+def test_forward_split3_vs_oracle(cuda, n, mode):
+    A = spd(6, n, seed=n)
+    iters = 12
+    reg = 0.01 if mode == capi.INIT_REFERENCE else 0.0
+    X = capi.newton_inverse_fwd(A.to(cuda), iters, init_mode=mode)
+    torch.cuda.synchronize()
+    assert capi.device_status() == 0
+    Xr = O.newton_fwd(A.numpy(), iters, mode=mode)
+    r_gpu = _res(A.numpy(), X.cpu().numpy(), reg)
+    r_ref = _res(A.numpy(), Xr, reg)
+    # residual within 1e-4 of the reference's
+    assert np.all(np.abs(r_gpu - r_ref) <= 1e-4), (r_gpu, r_ref)
+    scale = np.abs(Xr).max()
+    np.testing.assert_allclose(X.cpu().numpy(), Xr, rtol=0, atol=1e-4 * scale)
+
+
+def test_reference_entry_point_defaults(cuda):
+    A = spd(4, 128, seed=3).to(cuda)
+    X1 = capi.newton_inverse_fwd_reference(A, 12)
+    X2 = capi.newton_inverse_fwd(A, 12, init_mode=capi.INIT_REFERENCE, reg=0.01, precision=capi.PREC_SPLIT3)
+    torch.cuda.synchronize()
+    assert torch.equal(X1, X2)
+
+
+def test_config3_batch_residual(cuda):
+    # Configuration-3 matrices (128x128, sigma = 8, 1e-3 ridge), a 256-matrix
+    # slice, scaled-transpose init, 12 iterations.
+    from laplacianformer_b200 import workloads
+
+    A = workloads.config3(device=cuda, batch=256)["A"]
+    for prec in (capi.PREC_SPLIT3, capi.PREC_MIXED):
+        X = capi.newton_inverse_fwd(A, 12, init_mode=capi.INIT_SCALED_TRANSPOSE, precision=prec)
+        res = capi.newton_inverse_residual(A, X, 0.0)
+        torch.cuda.synchronize()
+        Xr = O.newton_fwd(A[:, :16].cpu().numpy(), 12, mode=O.INIT_SCALED_TRANSPOSE)
+        r_ref = _res(A[:, :16].cpu().numpy(), Xr, 0.0).ravel()
+        r_gpu = _res(A[:, :16].cpu().numpy(), X[:, :16].cpu().numpy(), 0.0).ravel()
+        assert np.all(np.abs(r_gpu - r_ref) <= 1e-4), (prec, r_gpu, r_ref)
+        # the device residual kernel agrees with the host computation
+        np.testing.assert_allclose(res.view(-1)[:16].cpu().numpy(), r_gpu, rtol=1e-2, atol=1e-5)
+
+
+@pytest.mark.parametrize("n", [5, 64, 128])
+def test_fp32_simt_mode(cuda, n):
+    A = spd(3, n, seed=40 + n)
+    X = capi.newton_inverse_fwd(A.to(cuda), 10, precision=capi.PREC_FP32_SIMT)
+    torch.cuda.synchronize()
+    Xr = O.newton_fwd(A.numpy(), 10, order=1)
+    np.testing.assert_allclose(X.cpu().numpy(), Xr, rtol=0, atol=2e-5 * np.abs(Xr).max())
+
+
+@pytest.mark.parametrize("n", [3, 64, 112, 128])
+def test_fp64(cuda, n):
+    A = spd(2, n, seed=60 + n).double()
+    X = capi.newton_inverse_fwd(A.to(cuda), 9)
+    torch.cuda.synchronize()
+    Xr = O.newton_fwd(A.numpy(), 9, order=1)
+    np.testing.assert_allclose(X.cpu().numpy(), Xr, rtol=1e-10, atol=1e-12 * np.abs(Xr).max())
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16], ids=str)
+def test_half_inputs(cuda, dtype):
+    A = spd(4, 49, seed=7)
+    Ah = A.to(dtype)
+    X = capi.newton_inverse_fwd(Ah.to(cuda), 8)
+    torch.cuda.synchronize()
+    Xr = O.newton_fwd(Ah.float().numpy(), 8)
+    Xr_t = torch.from_numpy(np.ascontiguousarray(Xr)).to(dtype).float().numpy()
+    np.testing.assert_allclose(X.float().cpu().numpy(), Xr_t, rtol=2e-2, atol=2e-2 * np.abs(Xr).max())
+
+
+def test_zero_iterations_returns_init(cuda):
+    A = spd(2, 30, seed=8)
+    X = capi.newton_inverse_fwd(A.to(cuda), 0)
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(X.cpu().numpy(), O.newton_fwd(A.numpy(), 0), rtol=1e-6, atol=1e-9)
+
+
+@pytest.mark.parametrize("n", [1, 33, 128])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float64, torch.float16], ids=str)
+def test_backward_vs_oracle(cuda, n, dtype):
+    g0 = torch.Generator().manual_seed(n)
+    V = torch.randn(2, 3, n, n, generator=g0, dtype=torch.float64).to(dtype)
+    G = torch.randn(2, 3, n, n, generator=g0, dtype=torch.float64).to(dtype)
+    dA = capi.newton_inverse_bwd(G.to(cuda), V.to(cuda))
+    torch.cuda.synchronize()
+    wide = torch.float64 if dtype == torch.float64 else torch.float32
+    ref = O.newton_bwd(G.to(wide).numpy(), V.to(wide).numpy())
+    tol = {torch.float32: 1e-5, torch.float64: 1e-12, torch.float16: 1e-2}[dtype]
+    scale = np.abs(ref).max() + 1e-30
+    np.testing.assert_allclose(dA.to(wide).cpu().numpy(), np.asarray(torch.tensor(ref).to(dtype).to(wide)), rtol=0, atol=tol * scale * 4)
+
+
+def test_unsupported_sizes(cuda):
+    assert capi.newton_inverse_supported(128)
+    assert not capi.newton_inverse_supported(129)
+    A = torch.randn(1, 1, 129, 129, device=cuda)
+    with pytest.raises(capi.LfError) as e:
+        capi.newton_inverse_fwd(A, 3)
+    assert e.value.code == capi.LF_ERR_UNSUPPORTED
+
+
+def test_extension_and_autograd(cuda, ext):
+    from laplacianformer_b200.ops import newton_inverse
+
+    A = spd(1, 64, seed=11).to(cuda)
+    out = torch.empty_like(A)
+    ext.NewtonInverse_forward(A, out, 10)
+    assert torch.equal(out, capi.newton_inverse_fwd_reference(A, 10))
+    assert ext.NewtonInverse_is_supported(128) and not ext.NewtonInverse_is_supported(129)
+    with pytest.raises(RuntimeError, match="not supported"):
+        big = torch.randn(1, 1, 130, 130, device=cuda)
+        ext.NewtonInverse_forward(big, torch.empty_like(big), 3)
+    Ad = A.double().requires_grad_()
+    X = newton_inverse(Ad, 30)
+    G = torch.randn_like(X)
+    X.backward(G)
+    Xd = X.detach()
+    expect = -(Xd.transpose(-1, -2) @ G @ Xd.transpose(-1, -2))
+    torch.testing.assert_close(Ad.grad, expect)
+
+
+def test_against_reference_module(cuda, ref_module):
+    if ref_module is None:
+        pytest.skip("oracle/_ref not built (python oracle/build_ref.py)")
+    for n, iters in ((64, 10), (128, 12), (49, 8)):
+        A = spd(8, n, seed=100 + n).to(cuda)
+        Xr = torch.empty_like(A)
+        ref_module.NewtonInverse_forward(A, Xr, iters)
+        X = capi.newton_inverse_fwd_reference(A, iters)
+        G = torch.randn_like(A)
+        dr = torch.empty_like(A)
+        ref_module.NewtonInverse_backward(G, Xr, dr)
+        d = capi.newton_inverse_bwd(G, Xr)
+        torch.cuda.synchronize()
+        r_ref = _res(A.cpu().numpy(), Xr.cpu().numpy(), 0.01)
+        r_gpu = _res(A.cpu().numpy(), X.cpu().numpy(), 0.01)
+        assert np.all(np.abs(r_gpu - r_ref) <= 1e-4), (n, r_gpu, r_ref)
+        torch.testing.assert_close(X, Xr, rtol=0, atol=1e-4 * Xr.abs().max().item())
+        torch.testing.assert_close(d, dr, rtol=0, atol=1e-5 * dr.abs().max().item())
