@@ -62,7 +62,7 @@ def test_config3_batch_residual(cuda):
         r_gpu = _res(A[:, :16].cpu().numpy(), X[:, :16].cpu().numpy(), 0.0).ravel()
         assert np.all(np.abs(r_gpu - r_ref) <= 1e-4), (prec, r_gpu, r_ref)
         # the device residual kernel agrees with the host computation
-        np.testing.assert_allclose(res.view(-1)[:16].cpu().numpy(), r_gpu, rtol=1e-2, atol=1e-5)
+        np.testing.assert_allclose(res.view(A.shape[0], A.shape[1])[:, :16].reshape(-1).cpu().numpy(), r_gpu, rtol=1e-2, atol=1e-5)
 
 
 @pytest.mark.parametrize("n", [5, 64, 128])
