@@ -375,6 +375,32 @@ def run_reference(args, rank, world, dev):
     }
 
 
+def run_only(args, dev):
+    """One workload, no sampling or baselines (for ncu launch lists and captures)."""
+    from laplacianformer_b200 import capi, workloads
+
+    stream = torch.cuda.current_stream(dev)
+    flush = _flush_buffer(dev)
+    if args.only == "laplace":
+        dtype = {"fp32": torch.float32, "fp16": torch.float16, "bf16": torch.bfloat16}[args.dtype]
+        w = workloads.config2(device=dev, dtype=dtype)
+        q, kT, ds = w["q"], w["kT"], w["ds"]
+        s = torch.empty(q.shape[0], q.shape[1], q.shape[2], kT.shape[3], device=dev, dtype=dtype)
+        dq, dk = torch.empty_like(q), torch.empty_like(kT)
+
+        def step():
+            capi.laplace_sub_fwd(q, kT, s)
+            capi.laplace_sub_bwd(ds, q, kT, dq, dk)
+    else:
+        A = workloads.config3(device=dev, batch=args.ns_batch)["A"]
+        X = torch.empty_like(A)
+
+        def step():
+            capi.newton_inverse_fwd(A, 12, init_mode=capi.INIT_SCALED_TRANSPOSE, out=X)
+    times = time_steps(step, args.steps, args.warmup, flush, stream)
+    print(json.dumps({"only": args.only, "ms_per_step": statistics.mean(times), "steps": args.steps}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -383,6 +409,9 @@ def main():
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--dtype", choices=["fp32", "fp16", "bf16"], default="fp32")
     ap.add_argument("--skip-newton", action="store_true")
+    ap.add_argument("--only", choices=["laplace", "newton"], default=None,
+                    help="profiling aid: run one workload only and print its timings")
+    ap.add_argument("--ns-batch", type=int, default=4096)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
@@ -400,6 +429,9 @@ def main():
         print(json.dumps(line), flush=True)
         return
 
+    if args.only:
+        run_only(args, dev)
+        return
     if world > 1:
         torch.distributed.init_process_group("nccl", device_id=dev)
     try:

@@ -77,6 +77,37 @@ __device__ __forceinline__ A absdiff_acc(A acc, A q, A k) {
     }
 }
 
+// acc[r][j] += |q[r][c] - k[j][c]| for the channels c of one 16-channel
+// chunk, in channel order.  FULL = 16 unrolls the whole chunk; FULL = 0 takes
+// the number of valid channels at run time (ragged last chunk).
+template <typename A, int TM, int MC, int FULL>
+__device__ __forceinline__ void accum_chunk(A (&acc)[TM][MC], const A (&qr)[TM][16], const A* kbase, int DP,
+                                            int valid = 16) {
+#pragma unroll
+    for (int j = 0; j < MC; ++j) {
+        const A* kr = kbase + j * DP;
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) {
+            if (!FULL && c4 * 4 >= valid) break;
+            A kv[4];
+            if constexpr (sizeof(A) == 4) {
+                float4 t = *reinterpret_cast<const float4*>(kr + 4 * c4);
+                kv[0] = t.x; kv[1] = t.y; kv[2] = t.z; kv[3] = t.w;
+            } else {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) kv[e] = kr[4 * c4 + e];
+            }
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                if (FULL || 4 * c4 + e < valid) {
+#pragma unroll
+                    for (int r = 0; r < TM; ++r) acc[r][j] = absdiff_acc<A>(acc[r][j], qr[r][4 * c4 + e], kv[e]);
+                }
+            }
+        }
+    }
+}
+
 // One CTA = kThreads*TM query rows of one (b,h); thread t owns rows
 // base + t + kThreads*r.  ks holds KT transposed to [m][DP] in the
 // accumulation type (DP = d rounded up to 16, zero padded).
@@ -125,30 +156,10 @@ lsub_fwd_kernel(const T* __restrict__ q, const T* __restrict__ kT, T* __restrict
                     for (int e = 0; e < 16; ++e) qr[r][e] = A(0);
                 }
             }
-            // Padded channels (c >= d) hold 0 in both operands: |0 - 0| adds +0.
-            const int cmax = valid < 16 ? valid : 16;
-#pragma unroll
-            for (int j = 0; j < MC; ++j) {
-                const A* kr = ks + (mc + j) * DP + dc;
-#pragma unroll
-                for (int c4 = 0; c4 < 4; ++c4) {
-                    if (c4 * 4 >= cmax) break;
-                    A kv[4];
-                    if constexpr (sizeof(A) == 4) {
-                        float4 t = *reinterpret_cast<const float4*>(kr + 4 * c4);
-                        kv[0] = t.x; kv[1] = t.y; kv[2] = t.z; kv[3] = t.w;
-                    } else {
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) kv[e] = kr[4 * c4 + e];
-                    }
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        if (4 * c4 + e < cmax) {
-#pragma unroll
-                            for (int r = 0; r < TM; ++r) acc[r][j] = absdiff_acc<A>(acc[r][j], qr[r][4 * c4 + e], kv[e]);
-                        }
-                    }
-                }
+            if (valid >= 16) {
+                accum_chunk<A, TM, MC, 16>(acc, qr, ks + mc * DP + dc, DP);
+            } else {
+                accum_chunk<A, TM, MC, 0>(acc, qr, ks + mc * DP + dc, DP, valid);
             }
         }
 #pragma unroll
@@ -226,19 +237,25 @@ __device__ __forceinline__ A step_of(A q, A k) {
     }
 }
 
-constexpr int kRowChunk = 32;  // query rows staged per pass
+constexpr int kRowChunk = 64;  // query rows staged per pass
 
 struct BwdGeom {
     int n, m, d;
-    int DB, MCN, RG;  // channel blocks (32 lanes), landmark chunks, row groups
+    int DBC;          // channel blocks (of 32 lanes) per CTA; grid.z covers the rest
+    int MCN, RG;      // landmark chunks, row groups
     int MP;           // landmark stride of the staged gradient tile
     int KSTR;         // row stride of the per-CTA dKT accumulator (odd, conflict free)
     int rows_per_cta;
 };
 
-// grid = (cs, bh), cluster = (cs, 1, 1).  CTA x of (b,h) handles query rows
-// [x*rows_per_cta, (x+1)*rows_per_cta).  Warp w works on channel block
-// w % DB, landmark chunk (w / DB) % MCN and row group w / (DB*MCN).
+// grid = (cs, bh, channel groups), cluster = (cs, 1, 1).  CTA x of (b,h)
+// handles query rows [x*rows_per_cta, (x+1)*rows_per_cta) for channels
+// [z*32*DBC, (z+1)*32*DBC).  Warp w works on channel block w % DBC, landmark
+// chunk (w / DBC) % MCN and row group w / (DBC*MCN).
+//
+// Per 64-row chunk the CTA stages 2*dS and Q in shared memory (coalesced row
+// loads), with the row sums sum_j dS (warp shuffles) and the per-landmark
+// column sums sum_i dS (shared atomics, accumulated over the CTA's rows).
 template <typename T, int MB, bool DQ, bool DK>
 __global__ void __launch_bounds__(kThreads, (DQ && sizeof(T) != 8) ? 2 : 1)
 lsub_bwd_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* __restrict__ kT,
@@ -247,29 +264,35 @@ lsub_bwd_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* __res
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const int n = geo.n, m = geo.m, d = geo.d;
     const int MP = geo.MP;
+    const int CW = geo.DBC * 32;  // channels per CTA
     // Shared memory carve-up (accumulation type):
-    //   gs   [kRowChunk][MP]   2*G of the staged rows (zero padded)
-    //   rsum [kRowChunk]       sum_j G of each staged row
-    //   dqb  [kRowChunk][d]    dQ partials when MCN > 1
-    //   csum [MP]              sum_i G of the CTA's rows, per landmark
-    //   dkb  [d][KSTR]         dKT partials of this CTA
+    //   gs   [kRowChunk][MP]   2*dS of the staged rows (zero padded)
+    //   qs   [kRowChunk][CW]   Q of the staged rows, this CTA's channels
+    //   rsum [kRowChunk]       sum_j dS of each staged row
+    //   dqb  [kRowChunk][CW]   dQ partials when MCN > 1
+    //   csum [MP]              sum_i dS over the CTA's rows, per landmark
+    //   dkb  [CW][KSTR]        dKT partials of this CTA
     A* gs = reinterpret_cast<A*>(smem_raw);
-    A* rsum = gs + kRowChunk * MP;
+    A* qs = gs + kRowChunk * MP;
+    A* rsum = qs + kRowChunk * CW;
     A* dqb = rsum + kRowChunk;
-    A* csum = dqb + (geo.MCN > 1 ? kRowChunk * d : 0);
+    A* csum = dqb + (geo.MCN > 1 ? kRowChunk * CW : 0);
     A* dkb = csum + MP;
 
     cg::cluster_group cluster = cg::this_cluster();
     const int bh = blockIdx.y;
     const int split = blockIdx.x;
+    const int c0 = blockIdx.z * CW;              // first channel of this CTA
+    const int cw = min(CW, d - c0);              // channels of this CTA
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int groups = geo.DB * geo.MCN;
-    const int db = warp % geo.DB;
-    const int mcb = (warp / geo.DB) % geo.MCN;
+    const int groups = geo.DBC * geo.MCN;
+    const int db = warp % geo.DBC;
+    const int mcb = (warp / geo.DBC) % geo.MCN;
     const int rg = warp / groups;
     const bool warp_active = rg < geo.RG;
-    const int c = db * 32 + lane;
-    const bool lane_active = warp_active && c < d;
+    const int cl = db * 32 + lane;               // channel within the CTA
+    const int c = c0 + cl;
+    const bool lane_active = warp_active && cl < cw;
     const int j0 = mcb * MB;
 
     const T* Gb = g + (int64_t)bh * n * m;
@@ -277,7 +300,7 @@ lsub_bwd_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* __res
     const T* Kb = kT + (int64_t)bh * d * m;
 
     if (DK) {
-        for (int e = threadIdx.x; e < d * geo.KSTR; e += kThreads) dkb[e] = A(0);
+        for (int e = threadIdx.x; e < CW * geo.KSTR; e += kThreads) dkb[e] = A(0);
         for (int e = threadIdx.x; e < MP; e += kThreads) csum[e] = A(0);
     }
 
@@ -297,34 +320,34 @@ lsub_bwd_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* __res
     for (int64_t rc = r_begin; rc < r_end; rc += kRowChunk) {
         const int rows = (int)((r_end - rc) < kRowChunk ? (r_end - rc) : kRowChunk);
         __syncthreads();  // previous chunk fully consumed
-        // Stage 2*G for the chunk (coalesced over the contiguous rows*m block).
-        const T* gsrc = Gb + rc * m;
-        for (int e = threadIdx.x; e < kRowChunk * MP; e += kThreads) {
-            int i = e / MP, j = e - i * MP;
-            A v = (i < rows && j < m) ? Elem<T>::load(gsrc[(int64_t)i * m + j]) : A(0);
-            gs[e] = v + v;
-        }
-        if (DQ && geo.MCN > 1)
-            for (int e = threadIdx.x; e < kRowChunk * d; e += kThreads) dqb[e] = A(0);
-        __syncthreads();
-        if (DQ && threadIdx.x < kRowChunk) {
-            A sacc = A(0);
-            for (int j = 0; j < m; ++j) sacc += gs[threadIdx.x * MP + j];
-            rsum[threadIdx.x] = sacc * A(0.5);
-        }
-        if (DK) {
-            for (int j = threadIdx.x; j < m; j += kThreads) {
-                A sacc = A(0);
-                for (int i = 0; i < rows; ++i) sacc += gs[i * MP + j];
-                csum[j] += sacc * A(0.5);
+        // Stage the chunk: warp w takes rows w, w+8, ...; lanes walk the row.
+        for (int i = warp; i < kRowChunk; i += kThreads / 32) {
+            const bool row_ok = i < rows;
+            const T* grow = Gb + (rc + i) * m;
+            A rs = A(0);
+            for (int j = lane; j < MP; j += 32) {
+                A v = (row_ok && j < m) ? Elem<T>::load(grow[j]) : A(0);
+                gs[i * MP + j] = v + v;
+                rs += v;
+                if (DK && row_ok && j < m) atomicAdd(&csum[j], v);
             }
+            if (DQ) {
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) rs += __shfl_xor_sync(0xffffffffu, rs, o);
+                if (lane == 0) rsum[i] = rs;
+            }
+            const T* qrow = Qb + (rc + i) * d + c0;
+            for (int x = lane; x < CW; x += 32)
+                qs[i * CW + x] = (row_ok && x < cw) ? Elem<T>::load(qrow[x]) : A(0);
+            if (DQ && geo.MCN > 1)
+                for (int x = lane; x < CW; x += 32) dqb[i * CW + x] = A(0);
         }
         __syncthreads();
 
         if (lane_active) {
 #pragma unroll 1
             for (int i = rg; i < rows; i += geo.RG) {
-                const A qv = Elem<T>::load(Qb[(rc + i) * d + c]);
+                const A qv = qs[i * CW + cl];
                 const A* grow = gs + i * MP + j0;
                 A dqa = A(0);
 #pragma unroll
@@ -348,15 +371,16 @@ lsub_bwd_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* __res
                     if (geo.MCN == 1) {
                         dq[((int64_t)bh * n + rc + i) * d + c] = Elem<T>::store(dqa - rsum[i]);
                     } else {
-                        atomicAdd(&dqb[i * d + c], mcb == 0 ? dqa - rsum[i] : dqa);
+                        atomicAdd(&dqb[i * CW + cl], mcb == 0 ? dqa - rsum[i] : dqa);
                     }
                 }
             }
         }
         if (DQ && geo.MCN > 1) {
             __syncthreads();
-            for (int e = threadIdx.x; e < rows * d; e += kThreads)
-                dq[((int64_t)bh * n + rc) * d + e] = Elem<T>::store(dqb[e]);
+            for (int i = warp; i < rows; i += kThreads / 32)
+                for (int x = lane; x < cw; x += 32)
+                    dq[((int64_t)bh * n + rc + i) * d + c0 + x] = Elem<T>::store(dqb[i * CW + x]);
         }
     }
 
@@ -367,11 +391,11 @@ lsub_bwd_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* __res
 #pragma unroll
         for (int jj = 0; jj < MB; ++jj) {
             int j = j0 + jj;
-            if (j < m) atomicAdd(&dkb[c * geo.KSTR + j], -dka[jj]);
+            if (j < m) atomicAdd(&dkb[cl * geo.KSTR + j], -dka[jj]);
         }
     }
     __syncthreads();
-    for (int e = threadIdx.x; e < d * m; e += kThreads) {
+    for (int e = threadIdx.x; e < cw * m; e += kThreads) {
         int cc = e / m, j = e - cc * m;
         dkb[cc * geo.KSTR + j] += csum[j];
     }
@@ -379,10 +403,10 @@ lsub_bwd_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* __res
     cluster.sync();
     const int cs = (int)cluster.num_blocks();
     const int rank = (int)cluster.block_rank();
-    const int total = d * m;
+    const int total = cw * m;
     const int per = (total + cs - 1) / cs;
     const int e0 = rank * per, e1 = min(total, e0 + per);
-    T* dkout = dk + (int64_t)bh * d * m;
+    T* dkout = dk + (int64_t)bh * d * m + (int64_t)c0 * m;
     for (int e = e0 + threadIdx.x; e < e1; e += kThreads) {
         int cc = e / m, j = e - cc * m;
         A sacc = A(0);
@@ -396,17 +420,15 @@ lsub_bwd_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* __res
 }
 
 // Landmark chunk per warp (MB) and number of chunks (mcn): least padding of m
-// subject to (channel blocks) x (chunks) <= warps per CTA; ties prefer chunks
-// of at most 52 landmarks (larger ones spill registers in the fused kernel),
-// then the larger chunk.
-int pick_mb(int64_t m, int64_t d, int& mcn) {
+// with at most 8 chunks; ties prefer chunks of at most 52 landmarks (larger
+// ones spill registers in the fused kernel), then the larger chunk.
+int pick_mb(int64_t m, int& mcn) {
     static const int cands[] = {8, 16, 24, 32, 40, 48, 52, 56, 64};
-    const int64_t db = (d + 31) / 32;
     int best = 0;
     int64_t best_pad = -1;
     for (int c : cands) {
         int64_t chunks = (m + c - 1) / c;
-        if (chunks * db > kThreads / 32) continue;
+        if (chunks > kThreads / 32) continue;
         int64_t pad = chunks * c;
         bool better = best_pad < 0 || pad < best_pad;
         if (!better && pad == best_pad) {
@@ -425,19 +447,20 @@ int launch_bwd_mb(const T* g, const T* q, const T* kT, T* dq, T* dk, int64_t bh,
     using A = typename Elem<T>::acc;
     BwdGeom geo;
     geo.n = (int)n; geo.m = (int)m; geo.d = (int)d;
-    geo.DB = (int)((d + 31) / 32);
+    const int DB = (int)((d + 31) / 32);
     geo.MCN = mcn;
-    if (geo.DB * geo.MCN > kThreads / 32) {
-        set_error("LaplaceSubtraction backward: d=%lld, m=%lld exceed one CTA's warps", (long long)d, (long long)m);
-        return LF_ERR_UNSUPPORTED;
-    }
-    geo.RG = (kThreads / 32) / (geo.DB * geo.MCN);
+    geo.DBC = (kThreads / 32) / mcn;
+    if (geo.DBC > DB) geo.DBC = DB;
+    if (geo.DBC < 1) geo.DBC = 1;
+    const int64_t dgroups = (DB + geo.DBC - 1) / geo.DBC;
+    geo.RG = (kThreads / 32) / (geo.DBC * geo.MCN);
     geo.MP = (int)(((m + 3) / 4) * 4);
     if (geo.MP < mcn * MB) geo.MP = mcn * MB;
     geo.KSTR = (int)(m | 1);
-    size_t smem = sizeof(A) * ((size_t)kRowChunk * geo.MP + kRowChunk +
-                               (geo.MCN > 1 ? (size_t)kRowChunk * d : 0) + geo.MP +
-                               (DK ? (size_t)d * geo.KSTR : 0));
+    const int CW = geo.DBC * 32;
+    size_t smem = sizeof(A) * ((size_t)kRowChunk * geo.MP + (size_t)kRowChunk * CW + kRowChunk +
+                               (geo.MCN > 1 ? (size_t)kRowChunk * CW : 0) + geo.MP +
+                               (DK ? (size_t)CW * geo.KSTR : 0));
     if (smem > (size_t)max_optin_smem()) {
         set_error("LaplaceSubtraction backward: needs %zu bytes of shared memory", smem);
         return LF_ERR_UNSUPPORTED;
@@ -445,20 +468,21 @@ int launch_bwd_mb(const T* g, const T* q, const T* kT, T* dq, T* dk, int64_t bh,
     // Split each (b,h) over a cluster of up to 8 CTAs along the rows, aiming
     // for at least two CTAs per SM in total.
     int sms = num_sms();
-    int64_t want = (2 * (int64_t)sms + bh - 1) / bh;
+    int64_t units = bh * dgroups;
+    int64_t want = (2 * (int64_t)sms + units - 1) / units;
     int64_t cs = want < 1 ? 1 : (want > 8 ? 8 : want);
     int64_t max_by_rows = (n + kRowChunk - 1) / kRowChunk;
     if (cs > max_by_rows) cs = max_by_rows < 1 ? 1 : max_by_rows;
     int64_t rpc = (n + cs - 1) / cs;
     rpc = ((rpc + kRowChunk - 1) / kRowChunk) * kRowChunk;
     geo.rows_per_cta = (int)rpc;
-    if (bh > 65535) { set_error("b*h = %lld exceeds 65535", (long long)bh); return LF_ERR_UNSUPPORTED; }
+    if (bh > 65535 || dgroups > 65535) { set_error("b*h = %lld exceeds 65535", (long long)bh); return LF_ERR_UNSUPPORTED; }
 
     auto kern = lsub_bwd_kernel<T, MB, DQ, DK>;
     if (smem > 48 * 1024)
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)cs, (unsigned)bh, 1);
+    cfg.gridDim = dim3((unsigned)cs, (unsigned)bh, (unsigned)dgroups);
     cfg.blockDim = dim3(kThreads, 1, 1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
@@ -486,10 +510,9 @@ int launch_bwd_t(const void* g, const void* q, const void* kT, void* dq, void* d
     T* DQp = static_cast<T*>(dq);
     T* DKp = static_cast<T*>(dk);
     int mcn = 1;
-    int mb = pick_mb(m, d, mcn);
+    int mb = pick_mb(m, mcn);
     if (mb == 0) {
-        set_error("LaplaceSubtraction backward: m=%lld with d=%lld exceeds one CTA (needs ceil(d/32)*ceil(m/64) <= 8)",
-                  (long long)m, (long long)d);
+        set_error("LaplaceSubtraction backward supports m <= 512 (got %lld)", (long long)m);
         return LF_ERR_UNSUPPORTED;
     }
 #define LF_BWD_CASE(MBV) case MBV: return launch_bwd_mb<T, MBV, DQ, DK>(G, Q, K, DQp, DKp, bh, n, m, d, mcn, st);
