@@ -77,17 +77,17 @@ __device__ __forceinline__ A absdiff_acc(A acc, A q, A k) {
     }
 }
 
-// acc[r][j] += |q[r][c] - k[j][c]| for the channels c of one 16-channel
-// chunk, in channel order.  FULL = 16 unrolls the whole chunk; FULL = 0 takes
-// the number of valid channels at run time (ragged last chunk).
-template <typename A, int TM, int MC, int FULL>
-__device__ __forceinline__ void accum_chunk(A (&acc)[TM][MC], const A (&qr)[TM][16], const A* kbase, int DP,
-                                            int valid = 16) {
+// acc[r][j] += |q[r][c] - k[j][c]| for the DR channels of one register
+// chunk, in channel order.  FULL unrolls the whole chunk; otherwise `valid`
+// channels (ragged last chunk) are taken at run time.
+template <typename A, int TM, int MC, int DR, bool FULL>
+__device__ __forceinline__ void accum_chunk(A (&acc)[TM][MC], const A (&qr)[TM][DR], const A* kbase, int DP,
+                                            int valid = DR) {
 #pragma unroll
     for (int j = 0; j < MC; ++j) {
         const A* kr = kbase + j * DP;
 #pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4) {
+        for (int c4 = 0; c4 < DR / 4; ++c4) {
             if (!FULL && c4 * 4 >= valid) break;
             A kv[4];
             if constexpr (sizeof(A) == 4) {
@@ -109,17 +109,22 @@ __device__ __forceinline__ void accum_chunk(A (&acc)[TM][MC], const A (&qr)[TM][
 }
 
 // One CTA = kThreads*TM query rows of one (b,h); thread t owns rows
-// base + t + kThreads*r.  ks holds KT transposed to [m][DP] in the
-// accumulation type (DP = d rounded up to 16, zero padded).
-template <typename T, int TM, int MC>
+// base + t + kThreads*r and keeps DR channels of each in registers.  When
+// d <= DR the rows are loaded once and zero padded to DR (padded channels add
+// |0 - 0| = +0, which leaves every sum unchanged); otherwise the channels are
+// walked in DR-wide chunks.  ks holds KT transposed to [m][DP] in the
+// accumulation type (DP = max(DR, d rounded up to 16), zero padded).
+template <typename T, int TM, int MC, int DR>
 __global__ void __launch_bounds__(kThreads)
 lsub_fwd_kernel(const T* __restrict__ q, const T* __restrict__ kT, T* __restrict__ s,
                 int n, int m, int d, int tiles_per_bh, bool vec) {
     using A = typename Elem<T>::acc;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     A* ks = reinterpret_cast<A*>(smem_raw);
-    const int DP = (d + 15) & ~15;
+    const int d16 = (d + 15) & ~15;
+    const int DP = d16 > DR ? ((d + DR - 1) / DR) * DR : DR;
     const int MP = ((m + MC - 1) / MC) * MC;
+    const bool single = d <= DR;
 
     const int bh = blockIdx.x / tiles_per_bh;
     const int tile = blockIdx.x - bh * tiles_per_bh;
@@ -136,6 +141,26 @@ lsub_fwd_kernel(const T* __restrict__ q, const T* __restrict__ kT, T* __restrict
     const T* Qb = q + (int64_t)bh * n * d;
     T* Sb = s + (int64_t)bh * n * m;
 
+    A qr[TM][DR];
+    auto load_q = [&](int dc) {
+#pragma unroll
+        for (int r = 0; r < TM; ++r) {
+            int64_t row = row0 + (int64_t)kThreads * r;
+#pragma unroll
+            for (int x = 0; x < DR / 16; ++x) {
+                A(&dst)[16] = *reinterpret_cast<A(*)[16]>(&qr[r][16 * x]);
+                const int valid = d - dc - 16 * x;
+                if (row < n && valid > 0) {
+                    load_chunk16<T>(Qb + row * d + dc + 16 * x, valid, vec, dst);
+                } else {
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) dst[e] = A(0);
+                }
+            }
+        }
+    };
+    if (single) load_q(0);
+
     for (int mc = 0; mc < m; mc += MC) {
         A acc[TM][MC];
 #pragma unroll
@@ -143,23 +168,13 @@ lsub_fwd_kernel(const T* __restrict__ q, const T* __restrict__ kT, T* __restrict
 #pragma unroll
             for (int j = 0; j < MC; ++j) acc[r][j] = A(0);
 
-        for (int dc = 0; dc < d; dc += 16) {
-            A qr[TM][16];
-            const int valid = d - dc;
-#pragma unroll
-            for (int r = 0; r < TM; ++r) {
-                int64_t row = row0 + (int64_t)kThreads * r;
-                if (row < n) {
-                    load_chunk16<T>(Qb + row * d + dc, valid, vec, qr[r]);
-                } else {
-#pragma unroll
-                    for (int e = 0; e < 16; ++e) qr[r][e] = A(0);
-                }
-            }
-            if (valid >= 16) {
-                accum_chunk<A, TM, MC, 16>(acc, qr, ks + mc * DP + dc, DP);
-            } else {
-                accum_chunk<A, TM, MC, 0>(acc, qr, ks + mc * DP + dc, DP, valid);
+        if (single) {
+            accum_chunk<A, TM, MC, DR, true>(acc, qr, ks + mc * DP, DP);
+        } else {
+            for (int dc = 0; dc < d; dc += DR) {
+                load_q(dc);
+                if (d - dc >= DR) accum_chunk<A, TM, MC, DR, true>(acc, qr, ks + mc * DP + dc, DP);
+                else accum_chunk<A, TM, MC, DR, false>(acc, qr, ks + mc * DP + dc, DP, d - dc);
             }
         }
 #pragma unroll
@@ -185,11 +200,12 @@ int pick_mc(int64_t m) {
     return best;
 }
 
-template <typename T, int TM, int MC>
+template <typename T, int TM, int MC, int DR>
 int launch_fwd_mc(const T* q, const T* kT, T* s, int64_t bh, int64_t n, int64_t m, int64_t d,
                   cudaStream_t st) {
     using A = typename Elem<T>::acc;
-    const int DP = (int)((d + 15) & ~15);
+    const int d16 = (int)((d + 15) & ~15);
+    const int DP = d16 > DR ? (int)(((d + DR - 1) / DR) * DR) : DR;
     const int MP = (int)(((m + MC - 1) / MC) * MC);
     size_t smem = (size_t)MP * DP * sizeof(A);
     if (smem > (size_t)max_optin_smem()) {
@@ -197,7 +213,7 @@ int launch_fwd_mc(const T* q, const T* kT, T* s, int64_t bh, int64_t n, int64_t 
                   (long long)m, (long long)d, smem);
         return LF_ERR_UNSUPPORTED;
     }
-    auto kern = lsub_fwd_kernel<T, TM, MC>;
+    auto kern = lsub_fwd_kernel<T, TM, MC, DR>;
     if (smem > 48 * 1024)
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     int tiles = (int)((n + kThreads * TM - 1) / (kThreads * TM));
@@ -208,19 +224,32 @@ int launch_fwd_mc(const T* q, const T* kT, T* s, int64_t bh, int64_t n, int64_t 
     return check_launch("lsub_fwd_kernel");
 }
 
+template <typename T, int TM, int DR>
+int launch_fwd_dr(const T* Q, const T* K, T* S, int64_t bh, int64_t n, int64_t m, int64_t d, cudaStream_t st) {
+    switch (pick_mc(m)) {
+        case 4: return launch_fwd_mc<T, TM, 4, DR>(Q, K, S, bh, n, m, d, st);
+        case 5: return launch_fwd_mc<T, TM, 5, DR>(Q, K, S, bh, n, m, d, st);
+        case 6: return launch_fwd_mc<T, TM, 6, DR>(Q, K, S, bh, n, m, d, st);
+        case 7: return launch_fwd_mc<T, TM, 7, DR>(Q, K, S, bh, n, m, d, st);
+        default: return launch_fwd_mc<T, TM, 8, DR>(Q, K, S, bh, n, m, d, st);
+    }
+}
+
+// Register chunk: the whole row when d <= 64 (16 / 32 channels x 2 rows, or
+// 64 channels x 1 row), 32-channel chunks beyond; fp64 uses 16 x 1.
 template <typename T>
 int launch_fwd(const void* q, const void* kT, void* s, int64_t bh, int64_t n, int64_t m, int64_t d,
                cudaStream_t st) {
     const T* Q = static_cast<const T*>(q);
     const T* K = static_cast<const T*>(kT);
     T* S = static_cast<T*>(s);
-    constexpr int TM = sizeof(T) == 8 ? 1 : 2;
-    switch (pick_mc(m)) {
-        case 4: return launch_fwd_mc<T, TM, 4>(Q, K, S, bh, n, m, d, st);
-        case 5: return launch_fwd_mc<T, TM, 5>(Q, K, S, bh, n, m, d, st);
-        case 6: return launch_fwd_mc<T, TM, 6>(Q, K, S, bh, n, m, d, st);
-        case 7: return launch_fwd_mc<T, TM, 7>(Q, K, S, bh, n, m, d, st);
-        default: return launch_fwd_mc<T, TM, 8>(Q, K, S, bh, n, m, d, st);
+    if constexpr (sizeof(T) == 8) {
+        return launch_fwd_dr<T, 1, 16>(Q, K, S, bh, n, m, d, st);
+    } else {
+        if (d <= 16) return launch_fwd_dr<T, 2, 16>(Q, K, S, bh, n, m, d, st);
+        if (d <= 32) return launch_fwd_dr<T, 2, 32>(Q, K, S, bh, n, m, d, st);
+        if (d <= 64) return launch_fwd_dr<T, 1, 64>(Q, K, S, bh, n, m, d, st);
+        return launch_fwd_dr<T, 2, 32>(Q, K, S, bh, n, m, d, st);
     }
 }
 
@@ -237,7 +266,8 @@ __device__ __forceinline__ A step_of(A q, A k) {
     }
 }
 
-constexpr int kRowChunk = 64;  // query rows staged per pass
+constexpr int kRowChunk = 64;       // query rows staged per pass
+constexpr int kMaxColChunks = 16;   // landmarks <= 512 = 16 x 32 lanes
 
 struct BwdGeom {
     int n, m, d;
@@ -272,12 +302,15 @@ lsub_bwd_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* __res
     //   dqb  [kRowChunk][CW]   dQ partials when MCN > 1
     //   csum [MP]              sum_i dS over the CTA's rows, per landmark
     //   dkb  [CW][KSTR]        dKT partials of this CTA
+    //   cpart[8][MP]           per-warp partial column sums (each (warp, j)
+    //                          is owned by one thread: no atomics)
     A* gs = reinterpret_cast<A*>(smem_raw);
     A* qs = gs + kRowChunk * MP;
     A* rsum = qs + kRowChunk * CW;
     A* dqb = rsum + kRowChunk;
     A* csum = dqb + (geo.MCN > 1 ? kRowChunk * CW : 0);
     A* dkb = csum + MP;
+    A* cpart = dkb + (DK ? CW * geo.KSTR : 0);  // [8 warps][MP] column-sum partials
 
     cg::cluster_group cluster = cg::this_cluster();
     const int bh = blockIdx.y;
@@ -302,6 +335,7 @@ lsub_bwd_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* __res
     if (DK) {
         for (int e = threadIdx.x; e < CW * geo.KSTR; e += kThreads) dkb[e] = A(0);
         for (int e = threadIdx.x; e < MP; e += kThreads) csum[e] = A(0);
+        for (int e = threadIdx.x; e < (kThreads / 32) * MP; e += kThreads) cpart[e] = A(0);
     }
 
     // Landmark values of this lane's channel and its dKT partials.
@@ -325,11 +359,15 @@ lsub_bwd_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* __res
             const bool row_ok = i < rows;
             const T* grow = Gb + (rc + i) * m;
             A rs = A(0);
-            for (int j = lane; j < MP; j += 32) {
-                A v = (row_ok && j < m) ? Elem<T>::load(grow[j]) : A(0);
-                gs[i * MP + j] = v + v;
-                rs += v;
-                if (DK && row_ok && j < m) atomicAdd(&csum[j], v);
+#pragma unroll
+            for (int u = 0; u < kMaxColChunks; ++u) {
+                const int j = lane + 32 * u;
+                if (j < MP) {
+                    A v = (row_ok && j < m) ? Elem<T>::load(grow[j]) : A(0);
+                    gs[i * MP + j] = v + v;
+                    rs += v;
+                    if (DK) cpart[warp * MP + j] += v;
+                }
             }
             if (DQ) {
 #pragma unroll
@@ -386,6 +424,12 @@ lsub_bwd_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* __res
 
     if (!DK) return;
 
+    __syncthreads();
+    for (int j = threadIdx.x; j < m; j += kThreads) {
+        A sacc = A(0);
+        for (int w = 0; w < kThreads / 32; ++w) sacc += cpart[w * MP + j];
+        csum[j] = sacc;
+    }
     // dKT[c][j] = csum[j] - sum_i 2g*t, first within the CTA ...
     if (lane_active) {
 #pragma unroll
@@ -460,7 +504,7 @@ int launch_bwd_mb(const T* g, const T* q, const T* kT, T* dq, T* dk, int64_t bh,
     const int CW = geo.DBC * 32;
     size_t smem = sizeof(A) * ((size_t)kRowChunk * geo.MP + (size_t)kRowChunk * CW + kRowChunk +
                                (geo.MCN > 1 ? (size_t)kRowChunk * CW : 0) + geo.MP +
-                               (DK ? (size_t)CW * geo.KSTR : 0));
+                               (DK ? (size_t)CW * geo.KSTR + (size_t)(kThreads / 32) * geo.MP : 0));
     if (smem > (size_t)max_optin_smem()) {
         set_error("LaplaceSubtraction backward: needs %zu bytes of shared memory", smem);
         return LF_ERR_UNSUPPORTED;
