@@ -35,6 +35,22 @@ namespace {
 
 constexpr int kThreads = 256;
 
+// Fraction of the machine's CTA slots that `total` CTAs keep busy over the
+// waves they need (1.0 = no partial last wave).
+inline double wave_efficiency(int64_t total, int64_t slots) {
+    if (total <= 0 || slots <= 0) return 0.0;
+    int64_t waves = (total + slots - 1) / slots;
+    return (double)total / (double)(waves * slots);
+}
+
+template <typename K>
+int64_t cta_slots(K kern, size_t smem) {
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem) != cudaSuccess || per_sm < 1)
+        per_sm = 1;
+    return (int64_t)per_sm * num_sms();
+}
+
 // ---------------------------------------------------------------------------
 // Forward
 // ---------------------------------------------------------------------------
@@ -201,13 +217,18 @@ int pick_mc(int64_t m) {
 }
 
 template <typename T, int TM, int MC, int DR>
-int launch_fwd_mc(const T* q, const T* kT, T* s, int64_t bh, int64_t n, int64_t m, int64_t d,
-                  cudaStream_t st) {
+size_t fwd_smem(int64_t m, int64_t d) {
     using A = typename Elem<T>::acc;
     const int d16 = (int)((d + 15) & ~15);
     const int DP = d16 > DR ? (int)(((d + DR - 1) / DR) * DR) : DR;
     const int MP = (int)(((m + MC - 1) / MC) * MC);
-    size_t smem = (size_t)MP * DP * sizeof(A);
+    return (size_t)MP * DP * sizeof(A);
+}
+
+template <typename T, int TM, int MC, int DR>
+int launch_fwd_mc(const T* q, const T* kT, T* s, int64_t bh, int64_t n, int64_t m, int64_t d,
+                  cudaStream_t st) {
+    size_t smem = fwd_smem<T, TM, MC, DR>(m, d);
     if (smem > (size_t)max_optin_smem()) {
         set_error("LaplaceSubtraction forward: m*d = %lld*%lld needs %zu bytes of shared memory",
                   (long long)m, (long long)d, smem);
@@ -224,19 +245,43 @@ int launch_fwd_mc(const T* q, const T* kT, T* s, int64_t bh, int64_t n, int64_t 
     return check_launch("lsub_fwd_kernel");
 }
 
-template <typename T, int TM, int DR>
-int launch_fwd_dr(const T* Q, const T* K, T* S, int64_t bh, int64_t n, int64_t m, int64_t d, cudaStream_t st) {
-    switch (pick_mc(m)) {
-        case 4: return launch_fwd_mc<T, TM, 4, DR>(Q, K, S, bh, n, m, d, st);
-        case 5: return launch_fwd_mc<T, TM, 5, DR>(Q, K, S, bh, n, m, d, st);
-        case 6: return launch_fwd_mc<T, TM, 6, DR>(Q, K, S, bh, n, m, d, st);
-        case 7: return launch_fwd_mc<T, TM, 7, DR>(Q, K, S, bh, n, m, d, st);
-        default: return launch_fwd_mc<T, TM, 8, DR>(Q, K, S, bh, n, m, d, st);
+// Two rows per thread amortise each landmark load over more terms; one row
+// per thread halves the CTA's rows.  Take one row only when that fills the
+// last wave of CTAs clearly better.
+template <typename T, int MC, int DR>
+int launch_fwd_tm(const T* Q, const T* K, T* S, int64_t bh, int64_t n, int64_t m, int64_t d, cudaStream_t st) {
+    if constexpr (DR <= 32) {
+        const size_t smem = fwd_smem<T, 2, MC, DR>(m, d);
+        if (smem <= (size_t)max_optin_smem()) {
+            auto k1 = lsub_fwd_kernel<T, 1, MC, DR>;
+            auto k2 = lsub_fwd_kernel<T, 2, MC, DR>;
+            if (smem > 48 * 1024) {
+                cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+                cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            }
+            double e1 = wave_efficiency(bh * ((n + kThreads - 1) / kThreads), cta_slots(k1, smem));
+            double e2 = wave_efficiency(bh * ((n + 2 * kThreads - 1) / (2 * kThreads)), cta_slots(k2, smem));
+            if (e1 > e2 + 0.05) return launch_fwd_mc<T, 1, MC, DR>(Q, K, S, bh, n, m, d, st);
+        }
+        return launch_fwd_mc<T, 2, MC, DR>(Q, K, S, bh, n, m, d, st);
+    } else {
+        return launch_fwd_mc<T, 1, MC, DR>(Q, K, S, bh, n, m, d, st);
     }
 }
 
-// Register chunk: the whole row when d <= 64 (16 / 32 channels x 2 rows, or
-// 64 channels x 1 row), 32-channel chunks beyond; fp64 uses 16 x 1.
+template <typename T, int DR>
+int launch_fwd_dr(const T* Q, const T* K, T* S, int64_t bh, int64_t n, int64_t m, int64_t d, cudaStream_t st) {
+    switch (pick_mc(m)) {
+        case 4: return launch_fwd_tm<T, 4, DR>(Q, K, S, bh, n, m, d, st);
+        case 5: return launch_fwd_tm<T, 5, DR>(Q, K, S, bh, n, m, d, st);
+        case 6: return launch_fwd_tm<T, 6, DR>(Q, K, S, bh, n, m, d, st);
+        case 7: return launch_fwd_tm<T, 7, DR>(Q, K, S, bh, n, m, d, st);
+        default: return launch_fwd_tm<T, 8, DR>(Q, K, S, bh, n, m, d, st);
+    }
+}
+
+// Register chunk: the whole row when d <= 64 (16 / 32 channels x 1-2 rows,
+// or 64 channels x 1 row), 32-channel chunks beyond; fp64 uses 16 channels.
 template <typename T>
 int launch_fwd(const void* q, const void* kT, void* s, int64_t bh, int64_t n, int64_t m, int64_t d,
                cudaStream_t st) {
@@ -244,12 +289,12 @@ int launch_fwd(const void* q, const void* kT, void* s, int64_t bh, int64_t n, in
     const T* K = static_cast<const T*>(kT);
     T* S = static_cast<T*>(s);
     if constexpr (sizeof(T) == 8) {
-        return launch_fwd_dr<T, 1, 16>(Q, K, S, bh, n, m, d, st);
+        return launch_fwd_dr<T, 16>(Q, K, S, bh, n, m, d, st);
     } else {
-        if (d <= 16) return launch_fwd_dr<T, 2, 16>(Q, K, S, bh, n, m, d, st);
-        if (d <= 32) return launch_fwd_dr<T, 2, 32>(Q, K, S, bh, n, m, d, st);
-        if (d <= 64) return launch_fwd_dr<T, 1, 64>(Q, K, S, bh, n, m, d, st);
-        return launch_fwd_dr<T, 2, 32>(Q, K, S, bh, n, m, d, st);
+        if (d <= 16) return launch_fwd_dr<T, 16>(Q, K, S, bh, n, m, d, st);
+        if (d <= 32) return launch_fwd_dr<T, 32>(Q, K, S, bh, n, m, d, st);
+        if (d <= 64) return launch_fwd_dr<T, 64>(Q, K, S, bh, n, m, d, st);
+        return launch_fwd_dr<T, 32>(Q, K, S, bh, n, m, d, st);
     }
 }
 
@@ -266,7 +311,7 @@ __device__ __forceinline__ A step_of(A q, A k) {
     }
 }
 
-constexpr int kRowChunk = 64;       // query rows staged per pass
+constexpr int kRowChunk = 64;       // query rows staged per pass (at most)
 constexpr int kMaxColChunks = 16;   // landmarks <= 512 = 16 x 32 lanes
 
 struct BwdGeom {
@@ -276,6 +321,7 @@ struct BwdGeom {
     int MP;           // landmark stride of the staged gradient tile
     int KSTR;         // row stride of the per-CTA dKT accumulator (odd, conflict free)
     int rows_per_cta;
+    int RC;           // query rows staged per pass (<= kRowChunk)
 };
 
 // grid = (cs, bh, channel groups), cluster = (cs, 1, 1).  CTA x of (b,h)
@@ -294,21 +340,22 @@ lsub_bwd_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* __res
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const int n = geo.n, m = geo.m, d = geo.d;
     const int MP = geo.MP;
+    const int RC = geo.RC;  // query rows staged per pass
     const int CW = geo.DBC * 32;  // channels per CTA
     // Shared memory carve-up (accumulation type):
-    //   gs   [kRowChunk][MP]   2*dS of the staged rows (zero padded)
-    //   qs   [kRowChunk][CW]   Q of the staged rows, this CTA's channels
-    //   rsum [kRowChunk]       sum_j dS of each staged row
-    //   dqb  [kRowChunk][CW]   dQ partials when MCN > 1
+    //   gs   [RC][MP]   2*dS of the staged rows (zero padded)
+    //   qs   [RC][CW]   Q of the staged rows, this CTA's channels
+    //   rsum [RC]       sum_j dS of each staged row
+    //   dqb  [RC][CW]   dQ partials when MCN > 1
     //   csum [MP]              sum_i dS over the CTA's rows, per landmark
     //   dkb  [CW][KSTR]        dKT partials of this CTA
     //   cpart[8][MP]           per-warp partial column sums (each (warp, j)
     //                          is owned by one thread: no atomics)
     A* gs = reinterpret_cast<A*>(smem_raw);
-    A* qs = gs + kRowChunk * MP;
-    A* rsum = qs + kRowChunk * CW;
-    A* dqb = rsum + kRowChunk;
-    A* csum = dqb + (geo.MCN > 1 ? kRowChunk * CW : 0);
+    A* qs = gs + RC * MP;
+    A* rsum = qs + RC * CW;
+    A* dqb = rsum + RC;
+    A* csum = dqb + (geo.MCN > 1 ? RC * CW : 0);
     A* dkb = csum + MP;
     A* cpart = dkb + (DK ? CW * geo.KSTR : 0);  // [8 warps][MP] column-sum partials
 
@@ -351,11 +398,11 @@ lsub_bwd_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* __res
     const int64_t r_begin = (int64_t)split * geo.rows_per_cta;
     const int64_t r_end = (r_begin + geo.rows_per_cta < (int64_t)n) ? r_begin + geo.rows_per_cta : (int64_t)n;
 
-    for (int64_t rc = r_begin; rc < r_end; rc += kRowChunk) {
-        const int rows = (int)((r_end - rc) < kRowChunk ? (r_end - rc) : kRowChunk);
+    for (int64_t rc = r_begin; rc < r_end; rc += RC) {
+        const int rows = (int)((r_end - rc) < RC ? (r_end - rc) : RC);
         __syncthreads();  // previous chunk fully consumed
         // Stage the chunk: warp w takes rows w, w+8, ...; lanes walk the row.
-        for (int i = warp; i < kRowChunk; i += kThreads / 32) {
+        for (int i = warp; i < RC; i += kThreads / 32) {
             const bool row_ok = i < rows;
             const T* grow = Gb + (rc + i) * m;
             A rs = A(0);
@@ -401,8 +448,8 @@ lsub_bwd_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* __res
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
                         const A t = step_of<A>(qv, kreg[j4 + e]);
-                        if (DQ) dqa = fma(gv[e], t, dqa);
-                        if (DK) dka[j4 + e] = fma(gv[e], t, dka[j4 + e]);
+                        if (DQ) dqa = fma_acc(gv[e], t, dqa);
+                        if (DK) dka[j4 + e] = fma_acc(gv[e], t, dka[j4 + e]);
                     }
                 }
                 if (DQ) {
@@ -502,29 +549,37 @@ int launch_bwd_mb(const T* g, const T* q, const T* kT, T* dq, T* dk, int64_t bh,
     if (geo.MP < mcn * MB) geo.MP = mcn * MB;
     geo.KSTR = (int)(m | 1);
     const int CW = geo.DBC * 32;
-    size_t smem = sizeof(A) * ((size_t)kRowChunk * geo.MP + (size_t)kRowChunk * CW + kRowChunk +
-                               (geo.MCN > 1 ? (size_t)kRowChunk * CW : 0) + geo.MP +
-                               (DK ? (size_t)CW * geo.KSTR + (size_t)(kThreads / 32) * geo.MP : 0));
+    auto smem_for = [&](int rc) {
+        return sizeof(A) * ((size_t)rc * geo.MP + (size_t)rc * CW + rc + (geo.MCN > 1 ? (size_t)rc * CW : 0) +
+                            geo.MP + (DK ? (size_t)CW * geo.KSTR + (size_t)(kThreads / 32) * geo.MP : 0));
+    };
+    geo.RC = kRowChunk;
+    while (geo.RC > 8 && smem_for(geo.RC) > (size_t)max_optin_smem()) geo.RC /= 2;
+    size_t smem = smem_for(geo.RC);
     if (smem > (size_t)max_optin_smem()) {
         set_error("LaplaceSubtraction backward: needs %zu bytes of shared memory", smem);
         return LF_ERR_UNSUPPORTED;
     }
-    // Split each (b,h) over a cluster of up to 8 CTAs along the rows, aiming
-    // for at least two CTAs per SM in total.
-    int sms = num_sms();
-    int64_t units = bh * dgroups;
-    int64_t want = (2 * (int64_t)sms + units - 1) / units;
-    int64_t cs = want < 1 ? 1 : (want > 8 ? 8 : want);
-    int64_t max_by_rows = (n + kRowChunk - 1) / kRowChunk;
-    if (cs > max_by_rows) cs = max_by_rows < 1 ? 1 : max_by_rows;
-    int64_t rpc = (n + cs - 1) / cs;
-    rpc = ((rpc + kRowChunk - 1) / kRowChunk) * kRowChunk;
-    geo.rows_per_cta = (int)rpc;
-    if (bh > 65535 || dgroups > 65535) { set_error("b*h = %lld exceeds 65535", (long long)bh); return LF_ERR_UNSUPPORTED; }
-
     auto kern = lsub_bwd_kernel<T, MB, DQ, DK>;
     if (smem > 48 * 1024)
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    // Split each (b,h) over a cluster of cs <= 8 CTAs along the rows; cs is
+    // chosen so that the CTAs fill whole waves of the machine's CTA slots
+    // (ties: fewer CTAs per cluster).
+    const int64_t units = bh * dgroups;
+    const int64_t slots = cta_slots(kern, smem);
+    const int64_t max_by_rows = (n + geo.RC - 1) / geo.RC;
+    int64_t cs = 1;
+    double best = -1.0;
+    for (int64_t c = 1; c <= 8 && c <= (max_by_rows < 1 ? 1 : max_by_rows); ++c) {
+        double eff = wave_efficiency(units * c, slots);
+        if (eff > best + 1e-9) { best = eff; cs = c; }
+    }
+    int64_t rpc = (n + cs - 1) / cs;
+    rpc = ((rpc + geo.RC - 1) / geo.RC) * geo.RC;
+    geo.rows_per_cta = (int)rpc;
+    if (bh > 65535 || dgroups > 65535) { set_error("b*h = %lld exceeds 65535", (long long)bh); return LF_ERR_UNSUPPORTED; }
+
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)cs, (unsigned)bh, (unsigned)dgroups);
     cfg.blockDim = dim3(kThreads, 1, 1);

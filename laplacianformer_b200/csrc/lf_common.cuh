@@ -68,6 +68,11 @@ template <> struct Elem<__nv_bfloat16> {
         default: lfb::set_error("unsupported dtype code %d", dtype); return LF_ERR_DTYPE; \
     }
 
+// Fused multiply-add in the accumulation type (explicit single/double forms,
+// so that float arguments never resolve to the double-precision overload).
+__device__ __forceinline__ float fma_acc(float a, float b, float c) { return __fmaf_rn(a, b, c); }
+__device__ __forceinline__ double fma_acc(double a, double b, double c) { return __fma_rn(a, b, c); }
+
 // Exact (IEEE, flush-to-zero) fp32 helpers with no contraction.
 __device__ __forceinline__ float sub_ftz(float a, float b) {
     float r;

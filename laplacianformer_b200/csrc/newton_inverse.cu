@@ -40,10 +40,10 @@ __device__ int g_ns_status = 0;
 
 namespace {
 
-constexpr int kNsThreads = 256;
+constexpr int kNsThreads = 512;
 constexpr int kTile = 128;                 // padded matrix size
 constexpr int kOpBytes = kTile * kTile * 2; // one fp16 operand (32 KB)
-constexpr int kTmemCols = 256;             // accumulator + fp32 V
+constexpr int kTmemCols = 512;             // W and Y accumulators + fp32 V (384 used)
 
 // ---------------------------------------------------------------------------
 // PTX wrappers (tcgen05, mbarrier, fences)
@@ -171,10 +171,6 @@ __device__ __forceinline__ uint64_t desc_a(uint32_t base, int ks) {
 __device__ __forceinline__ uint64_t desc_b(uint32_t base, int ks) {
     return make_desc(base + ks * 2048, 16384, 1024);
 }
-// Instruction descriptor: D f32, A/B f16, A K-major, B MN-major, N = 128, M = 128.
-constexpr uint32_t kIdesc = (1u << 4) | (0u << 7) | (0u << 10) | (0u << 15) | (1u << 16) |
-                            ((uint32_t)(kTile >> 3) << 17) | ((uint32_t)(kTile >> 4) << 24);
-
 // Power-of-two scale that maps max|x| into [2^14, 2^15); 1 for 0 or non-finite.
 __device__ __forceinline__ float split_scale(float mx) {
     if (!(mx > 0.f) || !isfinite(mx)) return 1.f;
@@ -204,49 +200,79 @@ __device__ __forceinline__ void split_store(unsigned char* hi_base, unsigned cha
     }
 }
 
+__device__ __forceinline__ void named_sync(int id, int count) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+__device__ __forceinline__ void named_arrive(int id, int count) {
+    asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 struct NsShared {
-    uint64_t bar;
+    uint64_t bar[3];            // W columns [0,64), W columns [64,128), Y
     uint32_t tmem_base;
-    int abort;
-    float red[kNsThreads / 32];
+    float red[kNsThreads / 32][4];
+    float rowpart[4][kTile];    // per column-group partial row sums of |V|
+    float rmax[4];              // per lane-quadrant max of the row sums
     float colsum[kTile];
-    float scal[8];
 };
 
-// Issue one 128x128x128 product into the accumulator: nterm = 1 (hi*hi) or
-// 3 (hi*hi + hi*lo + lo*hi).
-__device__ __forceinline__ void issue_gemm(uint32_t acc, uint32_t a_hi, uint32_t a_lo, uint32_t b_hi,
-                                           uint32_t b_lo, int nterm) {
-#pragma unroll
-    for (int ks = 0; ks < kTile / 16; ++ks) {
-        mma_f16(acc, desc_a(a_hi, ks), desc_b(b_hi, ks), kIdesc, ks > 0 ? 1u : 0u);
+// One K-range of a product into the accumulator: N columns (64 or 128),
+// nterm = 1 (hi*hi) or 3 (hi*hi + hi*lo + lo*hi).  b_* may point into the
+// second 64-column block for an N = 64 product.
+template <int N>
+__device__ __forceinline__ void issue_mma(uint32_t acc, uint32_t a_hi, uint32_t a_lo, uint32_t b_hi,
+                                          uint32_t b_lo, int ks0, int ks1, int nterm, bool first) {
+    constexpr uint32_t idesc = (1u << 4) | (1u << 16) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(kTile >> 4) << 24);
+    for (int ks = ks0; ks < ks1; ++ks) {
+        mma_f16(acc, desc_a(a_hi, ks), desc_b(b_hi, ks), idesc, (first && ks == ks0) ? 0u : 1u);
         if (nterm == 3) {
-            mma_f16(acc, desc_a(a_hi, ks), desc_b(b_lo, ks), kIdesc, 1u);
-            mma_f16(acc, desc_a(a_lo, ks), desc_b(b_hi, ks), kIdesc, 1u);
+            mma_f16(acc, desc_a(a_hi, ks), desc_b(b_lo, ks), idesc, 1u);
+            mma_f16(acc, desc_a(a_lo, ks), desc_b(b_hi, ks), idesc, 1u);
         }
     }
 }
 
-__device__ __forceinline__ float block_max(float v, NsShared& sh) {
+// Block-wide max of four values (two __syncthreads).
+__device__ __forceinline__ void block_max4(float (&v)[4], NsShared& sh) {
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    for (int k = 0; k < 4; ++k)
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v[k] = fmaxf(v[k], __shfl_xor_sync(0xffffffffu, v[k], o));
     const int warp = threadIdx.x >> 5;
-    __syncthreads();  // previous users of sh.red are done
-    if ((threadIdx.x & 31) == 0) sh.red[warp] = v;
     __syncthreads();
-    float m = sh.red[0];
+    if ((threadIdx.x & 31) == 0)
 #pragma unroll
-    for (int w = 1; w < kNsThreads / 32; ++w) m = fmaxf(m, sh.red[w]);
-    return m;
+        for (int k = 0; k < 4; ++k) sh.red[warp][k] = v[k];
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        float m = sh.red[0][k];
+        for (int w = 1; w < kNsThreads / 32; ++w) m = fmaxf(m, sh.red[w][k]);
+        v[k] = m;
+    }
 }
 
-// grid = batch, block = 256 threads (8 warps).  Warp w owns TMEM lanes
-// 32*(w%4).. (matrix rows) and columns 64*(w/4).. of the 128x128 tile.
+// Set-up staging tile: 128x128 fp32, element (i, c) at i*128 + swz(i, c).
+// The XOR keeps row writes (lanes over c) and column reads (lanes over i)
+// free of bank conflicts.
+__device__ __forceinline__ int stage_idx(int i, int c) { return i * kTile + (c ^ (i & 31) ^ ((c >> 5) & 3)); }
+
+// grid = batch, block = 512 threads (16 warps).  Warp w owns TMEM lanes
+// 32*(w%4).. (matrix rows) and the 32 columns 32*(w/4).. of the tile.
+//
+// Per iteration, with one thread issuing every MMA:
+//   W[:, 0:64]  = V P[:, 0:64]   -> bar[0]   (warps of column groups 0,1 convert it)
+//   W[:, 64:128]= V P[:, 64:128] -> bar[1]   (column groups 2,3), overlapping the first conversion
+//   Y  = W[:, 0:64] V[0:64, :]   issued as soon as groups 0,1 have stored their half of W,
+//      + W[:, 64:128] V[64:128,:] issued when groups 2,3 have     -> bar[2]
+//   V <- 2V - Y (all warps), new split scale from a block max.
+// W's split scale comes from the bound max|W| <= ||V||_inf * max|P| (known
+// before the product), so its conversion needs no reduction.
 template <typename T>
 __global__ void __launch_bounds__(kNsThreads, 1)
 ns_tc_fwd_kernel(const T* __restrict__ a, T* __restrict__ x, int n, int iters, int mode, float reg,
                  int precision) {
-    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    extern __shared__ __align__(16) unsigned char smem_raw[];  // re-aligned to 1024 below
     unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     unsigned char* Ph = base;
     unsigned char* Pl = base + 1 * kOpBytes;
@@ -258,26 +284,24 @@ ns_tc_fwd_kernel(const T* __restrict__ a, T* __restrict__ x, int n, int iters, i
     NsShared& sh = *reinterpret_cast<NsShared*>(base + 6 * kOpBytes);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int quad = warp & 3, half = warp >> 2;
-    const int row = quad * 32 + lane;  // the matrix row this thread owns in the epilogues
+    const int quad = warp & 3, cg = warp >> 2;
+    const int row = quad * 32 + lane;  // matrix row this thread owns in the epilogues
+    const int col0 = cg * 32;          // its 32 columns
     const int64_t mat = blockIdx.x;
     const T* A = a + mat * (int64_t)n * n;
     T* X = x + mat * (int64_t)n * n;
 
     if (tid == 0) {
-        mbar_init(&sh.bar, 1);
+        for (int b = 0; b < 3; ++b) mbar_init(&sh.bar[b], 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        sh.abort = 0;
     }
     if (tid < kTile) sh.colsum[tid] = 0.f;
     if (warp == 0) tmem_alloc(&sh.tmem_base, kTmemCols);
     __syncthreads();
 
-    // ---- set-up: P = A + reg I into the staging tile (swizzled fp32) -------
-    // Warp w loads rows w, w+8, ...; lane l holds columns 4l..4l+3.  Row sums
-    // (signed for alpha, absolute for ||P||_inf) by shuffles, column sums by
-    // per-lane accumulation.
-    float rowsum_max = -1e30f, rowabs_max = 0.f, pmax = 0.f;
+    // ---- set-up: P = A + reg I into the staging tile -------------------------
+    // Warp w loads rows w, w+16, ...; lane l holds columns 4l..4l+3.
+    float mx[4] = {-1e30f, 0.f, 0.f, 0.f};  // signed row sum, |row| sum, max|P|, |col| sum
     float colacc[4] = {0.f, 0.f, 0.f, 0.f};
     for (int i = warp; i < kTile; i += kNsThreads / 32) {
         float v[4];
@@ -287,67 +311,61 @@ ns_tc_fwd_kernel(const T* __restrict__ a, T* __restrict__ x, int n, int iters, i
             float t = 0.f;
             if (i < n && c < n) t = Elem<T>::load(A[(int64_t)i * n + c]) + (i == c ? reg : 0.f);
             v[e] = t;
-            stage[i * kTile + (c ^ (i & 31))] = t;
+            stage[stage_idx(i, c)] = t;
             colacc[e] += fabsf(t);
-            pmax = fmaxf(pmax, fabsf(t));
+            mx[2] = fmaxf(mx[2], fabsf(t));
         }
-        float rs = 0.f, ra = 0.f;
-        if (mode == LF_NS_INIT_REFERENCE) {
-            // sequential sum like compute_alpha (:92-98) is not needed for a
-            // max; any order of the 128 padded terms is used here.
-            rs = (v[0] + v[1]) + (v[2] + v[3]);
-        }
-        ra = (fabsf(v[0]) + fabsf(v[1])) + (fabsf(v[2]) + fabsf(v[3]));
+        float rs = (v[0] + v[1]) + (v[2] + v[3]);
+        float ra = (fabsf(v[0]) + fabsf(v[1])) + (fabsf(v[2]) + fabsf(v[3]));
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
             rs += __shfl_xor_sync(0xffffffffu, rs, o);
             ra += __shfl_xor_sync(0xffffffffu, ra, o);
         }
         if (i < n) {
-            rowsum_max = fmaxf(rowsum_max, rs);
-            rowabs_max = fmaxf(rowabs_max, ra);
+            mx[0] = fmaxf(mx[0], rs);
+            mx[1] = fmaxf(mx[1], ra);
         }
     }
 #pragma unroll
     for (int e = 0; e < 4; ++e) atomicAdd(&sh.colsum[4 * lane + e], colacc[e]);
-    // Reduce the three maxima.
-    const float g_rowsum = block_max(rowsum_max, sh);
-    const float g_rowabs = block_max(rowabs_max, sh);
-    const float g_pmax = block_max(pmax, sh);
-    float colmax = (tid < kTile) ? sh.colsum[tid] : 0.f;
-    const float g_colabs = block_max(colmax, sh);
+    __syncthreads();
+    if (tid < kTile) mx[3] = sh.colsum[tid];
+    block_max4(mx, sh);
+    const float pmax = mx[2];
+    const float v0_scale = (mode == LF_NS_INIT_REFERENCE) ? __fdiv_rn(1.8f, mx[0] * mx[0])
+                                                         : __fdiv_rn(1.0f, mx[3] * mx[1]);
+    const float sP = split_scale(pmax);
+    float sV = split_scale(pmax * fabsf(v0_scale));
+    // ||V0||_inf: alpha*||P||_inf, or c*||P||_1 for V0 = c P^T.
+    float vinf = fabsf(v0_scale) * (mode == LF_NS_INIT_REFERENCE ? mx[1] : mx[3]);
 
-    float v0_scale;  // V0 = v0_scale * P (or P^T)
-    if (mode == LF_NS_INIT_REFERENCE) {
-        v0_scale = __fdiv_rn(1.8f, g_rowsum * g_rowsum);
-    } else {
-        v0_scale = __fdiv_rn(1.0f, g_colabs * g_rowabs);
-    }
-    const float sP = split_scale(g_pmax);
-    float sV = split_scale(g_pmax * fabsf(v0_scale));
-
-    // Each thread converts its row segment: P -> (Ph, Pl), V0 -> (Vh, Vl) and
-    // the fp32 V0 -> TMEM columns [128, 256).
     tc_fence_after();
     const uint32_t tmem = sh.tmem_base;
     const uint32_t t_lane = (uint32_t)(quad * 32) << 16;
-    const uint32_t t_acc = tmem + t_lane;            // accumulator columns [0,128)
-    const uint32_t t_v = tmem + t_lane + kTile;      // fp32 V columns [128,256)
-    for (int cb = 0; cb < 2; ++cb) {
-        const int col0 = half * 64 + cb * 32;
+    const uint32_t t_w = tmem + t_lane;              // W accumulator, columns [0,128)
+    const uint32_t t_y = tmem + t_lane + kTile;      // Y accumulator, columns [128,256)
+    const uint32_t t_v = tmem + t_lane + 2 * kTile;  // fp32 V, columns [256,384)
+    {
         float pv[32], vv[32];
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
             int c = col0 + e;
-            pv[e] = stage[row * kTile + (c ^ (row & 31))];
-            float src = (mode == LF_NS_INIT_REFERENCE) ? pv[e] : stage[c * kTile + (row ^ (c & 31))];
+            pv[e] = stage[stage_idx(row, c)];
+            float src = (mode == LF_NS_INIT_REFERENCE) ? pv[e] : stage[stage_idx(c, row)];
             vv[e] = src * v0_scale;
         }
         split_store(Ph, Pl, row, col0, pv, sP);
-        if (iters > 0) split_store(Vh, Vl, row, col0, vv, sV);
-        tmem_st32(t_v + col0, vv);
+        if (iters > 0) {
+            split_store(Vh, Vl, row, col0, vv, sV);
+            tmem_st32(t_v + col0, vv);
+            tmem_wait_st();
+        } else if (row < n) {
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+                if (col0 + e < n) X[(int64_t)row * n + col0 + e] = Elem<T>::store(vv[e]);
+        }
     }
-    tmem_wait_st();
     fence_async_smem();
     tc_fence_before();
     __syncthreads();  // staging reads done before W is overwritten; operands visible
@@ -357,112 +375,104 @@ ns_tc_fwd_kernel(const T* __restrict__ a, T* __restrict__ x, int n, int iters, i
     uint32_t phase = 0;
     bool ok = true;
 
-    for (int it = 0; it < iters && ok; ++it) {
+    for (int it = 0; it < iters; ++it) {
         const int nterm = (precision == LF_NS_PREC_MIXED && it < iters - 2) ? 1 : 3;
         const bool last = (it == iters - 1);
-        // ---- W = V P ----------------------------------------------------
+        const float sW = split_scale(vinf * pmax);
+        // ---- W = V P in two column halves ---------------------------------
         if (tid == 0) {
             tc_fence_after();
-            issue_gemm(tmem, aVh, aVl, aPh, aPl, nterm);
-            mma_commit(&sh.bar);
+            issue_mma<64>(tmem, aVh, aVl, aPh, aPl, 0, kTile / 16, nterm, true);
+            mma_commit(&sh.bar[0]);
+            issue_mma<64>(tmem + 64, aVh, aVl, aPh + 16384, aPl + 16384, 0, kTile / 16, nterm, true);
+            mma_commit(&sh.bar[1]);
         }
-        ok = !__syncthreads_or(!mbar_wait(&sh.bar, phase));
+        const bool lo_half = cg < 2;
+        bool okw = mbar_wait(&sh.bar[lo_half ? 0 : 1], phase);
+        tc_fence_after();
+        {
+            float wv[32];
+            tmem_ld32(t_w + col0, wv);
+            tmem_wait_ld();
+            reg_fence(wv);
+            const float iv = 1.f / sV, ip = 1.f / sP;
+#pragma unroll
+            for (int e = 0; e < 32; ++e) wv[e] = wv[e] * iv * ip;
+            split_store(Wh, Wl, row, col0, wv, sW);
+        }
+        fence_async_smem();
+        tc_fence_before();
+        // ---- Y = W V, K split so that the first half starts early ----------
+        if (lo_half) {
+            named_sync(1, kNsThreads / 2);
+            if (tid == 0) {
+                tc_fence_after();
+                issue_mma<128>(tmem + kTile, aWh, aWl, aVh, aVl, 0, kTile / 32, nterm, true);
+            }
+            if (warp == 0) {
+                named_sync(2, kNsThreads / 2 + 32);
+                if (lane == 0) {
+                    tc_fence_after();
+                    issue_mma<128>(tmem + kTile, aWh, aWl, aVh, aVl, kTile / 32, kTile / 16, nterm, false);
+                    mma_commit(&sh.bar[2]);
+                }
+                __syncwarp();
+            }
+        } else {
+            named_arrive(2, kNsThreads / 2 + 32);
+        }
+        okw = mbar_wait(&sh.bar[2], phase) && okw;
         phase ^= 1;
+        ok = !__syncthreads_or(!okw);
         if (!ok) break;
         tc_fence_after();
-        const float inv_v = 1.f / sV, inv_p = 1.f / sP;
-        float wv[2][32];
-        float wmax = 0.f;
-#pragma unroll
-        for (int cb = 0; cb < 2; ++cb) {
-            tmem_ld32(t_acc + half * 64 + cb * 32, wv[cb]);
-        }
-        tmem_wait_ld();
-        reg_fence(wv[0]);
-        reg_fence(wv[1]);
-#pragma unroll
-        for (int cb = 0; cb < 2; ++cb)
+        // ---- V <- 2V - Y ----------------------------------------------------
+        float vn[32];
+        float lmax = 0.f, lsum = 0.f;
+        {
+            float yv[32];
+            tmem_ld32(t_y + col0, yv);
+            tmem_ld32(t_v + col0, vn);
+            tmem_wait_ld();
+            reg_fence(yv);
+            reg_fence(vn);
+            const float iw = 1.f / sW, iv = 1.f / sV;
 #pragma unroll
             for (int e = 0; e < 32; ++e) {
-                wv[cb][e] = wv[cb][e] * inv_v * inv_p;
-                wmax = fmaxf(wmax, fabsf(wv[cb][e]));
+                vn[e] = fmaf(2.f, vn[e], -(yv[e] * iw * iv));
+                lmax = fmaxf(lmax, fabsf(vn[e]));
+                lsum += fabsf(vn[e]);
             }
-        const float sW = split_scale(block_max(wmax, sh));
+        }
+        if (last) {
+            if (row < n) {
 #pragma unroll
-        for (int cb = 0; cb < 2; ++cb) split_store(Wh, Wl, row, half * 64 + cb * 32, wv[cb], sW);
+                for (int e = 0; e < 32; ++e)
+                    if (col0 + e < n) X[(int64_t)row * n + col0 + e] = Elem<T>::store(vn[e]);
+            }
+            break;
+        }
+        tmem_st32(t_v + col0, vn);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) lmax = fmaxf(lmax, __shfl_xor_sync(0xffffffffu, lmax, o));
+        if (lane == 0) sh.red[warp][0] = lmax;
+        sh.rowpart[cg][row] = lsum;
+        __syncthreads();
+        float m = sh.red[0][0];
+        for (int w = 1; w < kNsThreads / 32; ++w) m = fmaxf(m, sh.red[w][0]);
+        sV = split_scale(m);
+        if (cg == 0) {
+            float rs = sh.rowpart[0][row] + sh.rowpart[1][row] + sh.rowpart[2][row] + sh.rowpart[3][row];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) rs = fmaxf(rs, __shfl_xor_sync(0xffffffffu, rs, o));
+            if (lane == 0) sh.rmax[quad] = rs;
+        }
+        split_store(Vh, Vl, row, col0, vn, sV);
+        tmem_wait_st();
         fence_async_smem();
         tc_fence_before();
         __syncthreads();
-        // ---- Y = W V ----------------------------------------------------
-        if (tid == 0) {
-            tc_fence_after();
-            issue_gemm(tmem, aWh, aWl, aVh, aVl, nterm);
-            mma_commit(&sh.bar);
-        }
-        ok = !__syncthreads_or(!mbar_wait(&sh.bar, phase));
-        phase ^= 1;
-        if (!ok) break;
-        tc_fence_after();
-        const float inv_w = 1.f / sW, inv_v2 = 1.f / sV;
-        float vmax = 0.f;
-#pragma unroll
-        for (int cb = 0; cb < 2; ++cb) {
-            float yv[32], vo[32];
-            tmem_ld32(t_acc + half * 64 + cb * 32, yv);
-            tmem_ld32(t_v + half * 64 + cb * 32, vo);
-            tmem_wait_ld();
-            reg_fence(yv);
-            reg_fence(vo);
-#pragma unroll
-            for (int e = 0; e < 32; ++e) {
-                float vn = fmaf(2.f, vo[e], -(yv[e] * inv_w * inv_v2));
-                wv[cb][e] = vn;
-                vmax = fmaxf(vmax, fabsf(vn));
-            }
-            if (!last) tmem_st32(t_v + half * 64 + cb * 32, wv[cb]);
-        }
-        if (!last) {
-            tmem_wait_st();
-            sV = split_scale(block_max(vmax, sh));
-#pragma unroll
-            for (int cb = 0; cb < 2; ++cb) split_store(Vh, Vl, row, half * 64 + cb * 32, wv[cb], sV);
-            fence_async_smem();
-            tc_fence_before();
-            __syncthreads();
-        } else {
-            // Final iterate straight to global memory.
-            if (row < n) {
-#pragma unroll
-                for (int cb = 0; cb < 2; ++cb)
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) {
-                        int c = half * 64 + cb * 32 + e;
-                        if (c < n) X[(int64_t)row * n + c] = Elem<T>::store(wv[cb][e]);
-                    }
-            }
-        }
-    }
-    if (iters <= 0) {
-        // No iteration: the output is V0.
-        if (row < n) {
-            for (int cb = 0; cb < 2; ++cb) {
-                float vv[32];
-                tmem_ld32(t_v + half * 64 + cb * 32, vv);
-                tmem_wait_ld();
-                reg_fence(vv);
-#pragma unroll
-                for (int e = 0; e < 32; ++e) {
-                    int c = half * 64 + cb * 32 + e;
-                    if (c < n) X[(int64_t)row * n + c] = Elem<T>::store(vv[e]);
-                }
-            }
-        } else {
-            for (int cb = 0; cb < 2; ++cb) {
-                float vv[32];
-                tmem_ld32(t_v + half * 64 + cb * 32, vv);
-                tmem_wait_ld();
-            }
-        }
+        vinf = fmaxf(fmaxf(sh.rmax[0], sh.rmax[1]), fmaxf(sh.rmax[2], sh.rmax[3]));
     }
     if (!ok && tid == 0) atomicExch(&g_ns_status, (int)LF_ERR_TIMEOUT);
     tc_fence_before();
@@ -547,7 +557,7 @@ ns_simt_fwd_kernel(const T* __restrict__ a, T* __restrict__ x, int n, int iters,
             for (int j = tj; j < n; j += tpr) {
                 Acc acc = 0;
                 if (r < n)
-                    for (int k = 0; k < n; ++k) acc = fma(V[r * S + k], P(k, j), acc);
+                    for (int k = 0; k < n; ++k) acc = fma_acc(V[r * S + k], P(k, j), acc);
                 Wr[rr * S + j] = acc;
             }
             __syncthreads();
@@ -555,8 +565,8 @@ ns_simt_fwd_kernel(const T* __restrict__ a, T* __restrict__ x, int n, int iters,
             if (r < n) {
                 for (int j = tj; j < n; j += tpr) {
                     Acc acc = 0;
-                    for (int k = 0; k < n; ++k) acc = fma(Wr[rr * S + k], V[k * S + j], acc);
-                    Acc vn = fma(Acc(2), V[r * S + j], -acc);
+                    for (int k = 0; k < n; ++k) acc = fma_acc(Wr[rr * S + k], V[k * S + j], acc);
+                    Acc vn = fma_acc(Acc(2), V[r * S + j], -acc);
                     if (NEWV_GLOBAL) X[(int64_t)r * n + j] = (T)vn;
                     else Vn[r * S + j] = vn;
                 }
@@ -608,14 +618,14 @@ ns_simt_bwd_kernel(const T* __restrict__ g, const T* __restrict__ v, T* __restri
         for (int j = tj; j < n; j += tpr) {
             Acc acc = 0;
             if (r < n)
-                for (int p = 0; p < n; ++p) acc = fma(V[p * S + r], (Acc)Elem<T>::load(G[(int64_t)p * n + j]), acc);
+                for (int p = 0; p < n; ++p) acc = fma_acc(V[p * S + r], (Acc)Elem<T>::load(G[(int64_t)p * n + j]), acc);
             Tr[rr * S + j] = acc;
         }
         __syncthreads();
         if (r < n) {
             for (int j = tj; j < n; j += tpr) {
                 Acc acc = 0;
-                for (int k = 0; k < n; ++k) acc = fma(Tr[rr * S + k], V[j * S + k], acc);
+                for (int k = 0; k < n; ++k) acc = fma_acc(Tr[rr * S + k], V[j * S + k], acc);
                 O[(int64_t)r * n + j] = Elem<T>::store(-acc);
             }
         }
@@ -636,10 +646,10 @@ ns_residual_kernel(const T* __restrict__ a, const T* __restrict__ x, Acc* __rest
         int i = e / n, j = e - i * n;
         Acc acc = 0;
         for (int k = 0; k < n; ++k)
-            acc = fma((Acc)Elem<T>::load(A[(int64_t)i * n + k]) + (i == k ? reg : Acc(0)),
+            acc = fma_acc((Acc)Elem<T>::load(A[(int64_t)i * n + k]) + (i == k ? reg : Acc(0)),
                       (Acc)Elem<T>::load(X[(int64_t)k * n + j]), acc);
         acc -= (i == j) ? Acc(1) : Acc(0);
-        ss = fma(acc, acc, ss);
+        ss = fma_acc(acc, acc, ss);
     }
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
