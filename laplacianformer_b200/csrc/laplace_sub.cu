@@ -25,6 +25,7 @@
 //   and add their dKT partials through distributed shared memory; no atomics
 //   in global memory and no pre-zeroed output.
 #include <cooperative_groups.h>
+#include <stdlib.h>
 
 #include "lf_common.cuh"
 
@@ -311,6 +312,39 @@ __device__ __forceinline__ A step_of(A q, A k) {
     }
 }
 
+// Four backward terms (landmarks j..j+3 of one channel) in fp32: for each,
+// d = q - k, t = sat(d*2^125 + 1/2), dq += g*t, dk_j += g*t — exactly four
+// FP32-pipe instructions per term, written out so that nothing else is
+// scheduled into the hot loop.
+template <bool DQ, bool DK>
+__device__ __forceinline__ void bwd_quad(float q, float k0, float k1, float k2, float k3, const float (&g)[4],
+                                         float& dq, float& a0, float& a1, float& a2, float& a3) {
+    float t0, t1, t2, t3;
+    asm("{\n\t.reg .f32 d0, d1, d2, d3;\n\t"
+        "sub.rn.ftz.f32 d0, %4, %5;\n\t"
+        "sub.rn.ftz.f32 d1, %4, %6;\n\t"
+        "sub.rn.ftz.f32 d2, %4, %7;\n\t"
+        "sub.rn.ftz.f32 d3, %4, %8;\n\t"
+        "fma.rn.ftz.sat.f32 %0, d0, 0f7E000000, 0f3F000000;\n\t"
+        "fma.rn.ftz.sat.f32 %1, d1, 0f7E000000, 0f3F000000;\n\t"
+        "fma.rn.ftz.sat.f32 %2, d2, 0f7E000000, 0f3F000000;\n\t"
+        "fma.rn.ftz.sat.f32 %3, d3, 0f7E000000, 0f3F000000;\n\t}"
+        : "=f"(t0), "=f"(t1), "=f"(t2), "=f"(t3)
+        : "f"(q), "f"(k0), "f"(k1), "f"(k2), "f"(k3));
+    if (DQ) {
+        dq = __fmaf_rn(g[0], t0, dq);
+        dq = __fmaf_rn(g[1], t1, dq);
+        dq = __fmaf_rn(g[2], t2, dq);
+        dq = __fmaf_rn(g[3], t3, dq);
+    }
+    if (DK) {
+        a0 = __fmaf_rn(g[0], t0, a0);
+        a1 = __fmaf_rn(g[1], t1, a1);
+        a2 = __fmaf_rn(g[2], t2, a2);
+        a3 = __fmaf_rn(g[3], t3, a3);
+    }
+}
+
 constexpr int kRowChunk = 64;       // query rows staged per pass (at most)
 constexpr int kMaxColChunks = 16;   // landmarks <= 512 = 16 x 32 lanes
 
@@ -332,8 +366,8 @@ struct BwdGeom {
 // Per 64-row chunk the CTA stages 2*dS and Q in shared memory (coalesced row
 // loads), with the row sums sum_j dS (warp shuffles) and the per-landmark
 // column sums sum_i dS (shared atomics, accumulated over the CTA's rows).
-template <typename T, int MB, bool DQ, bool DK>
-__global__ void __launch_bounds__(kThreads, (DQ && sizeof(T) != 8) ? 2 : 1)
+template <typename T, int MB, bool DQ, bool DK, int MINB>
+__global__ void __launch_bounds__(kThreads, MINB)
 lsub_bwd_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* __restrict__ kT,
                 T* __restrict__ dq, T* __restrict__ dk, BwdGeom geo) {
     using A = typename Elem<T>::acc;
@@ -445,11 +479,16 @@ lsub_bwd_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* __res
 #pragma unroll
                         for (int e = 0; e < 4; ++e) gv[e] = grow[j4 + e];
                     }
+                    if constexpr (sizeof(A) == 4) {
+                        bwd_quad<DQ, DK>(qv, kreg[j4], kreg[j4 + 1], kreg[j4 + 2], kreg[j4 + 3], gv, dqa,
+                                         dka[j4], dka[j4 + 1], dka[j4 + 2], dka[j4 + 3]);
+                    } else {
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const A t = step_of<A>(qv, kreg[j4 + e]);
-                        if (DQ) dqa = fma_acc(gv[e], t, dqa);
-                        if (DK) dka[j4 + e] = fma_acc(gv[e], t, dka[j4 + e]);
+                        for (int e = 0; e < 4; ++e) {
+                            const A t = step_of<A>(qv, kreg[j4 + e]);
+                            if (DQ) dqa = fma_acc(gv[e], t, dqa);
+                            if (DK) dka[j4 + e] = fma_acc(gv[e], t, dka[j4 + e]);
+                        }
                     }
                 }
                 if (DQ) {
@@ -532,7 +571,7 @@ int pick_mb(int64_t m, int& mcn) {
     return best;
 }
 
-template <typename T, int MB, bool DQ, bool DK>
+template <typename T, int MB, bool DQ, bool DK, int MINB>
 int launch_bwd_mb(const T* g, const T* q, const T* kT, T* dq, T* dk, int64_t bh, int64_t n,
                   int64_t m, int64_t d, int mcn, cudaStream_t st) {
     using A = typename Elem<T>::acc;
@@ -560,7 +599,7 @@ int launch_bwd_mb(const T* g, const T* q, const T* kT, T* dq, T* dk, int64_t bh,
         set_error("LaplaceSubtraction backward: needs %zu bytes of shared memory", smem);
         return LF_ERR_UNSUPPORTED;
     }
-    auto kern = lsub_bwd_kernel<T, MB, DQ, DK>;
+    auto kern = lsub_bwd_kernel<T, MB, DQ, DK, MINB>;
     if (smem > 48 * 1024)
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     // Split each (b,h) over a cluster of cs <= 8 CTAs along the rows; cs is
@@ -614,7 +653,16 @@ int launch_bwd_t(const void* g, const void* q, const void* kT, void* dq, void* d
         set_error("LaplaceSubtraction backward supports m <= 512 (got %lld)", (long long)m);
         return LF_ERR_UNSUPPORTED;
     }
-#define LF_BWD_CASE(MBV) case MBV: return launch_bwd_mb<T, MBV, DQ, DK>(G, Q, K, DQp, DKp, bh, n, m, d, mcn, st);
+    static const int minb_env = [] {
+        const char* e = getenv("LFB_BWD_MINB");
+        return e ? atoi(e) : 2;
+    }();
+    constexpr int kMinb = (DQ && sizeof(T) != 8) ? 2 : 1;
+#define LF_BWD_CASE(MBV)                                                                              \
+    case MBV:                                                                                         \
+        if (kMinb == 2 && minb_env == 1)                                                              \
+            return launch_bwd_mb<T, MBV, DQ, DK, 1>(G, Q, K, DQp, DKp, bh, n, m, d, mcn, st);          \
+        return launch_bwd_mb<T, MBV, DQ, DK, kMinb>(G, Q, K, DQp, DKp, bh, n, m, d, mcn, st);
     switch (mb) {
         LF_BWD_CASE(8) LF_BWD_CASE(16) LF_BWD_CASE(24) LF_BWD_CASE(32) LF_BWD_CASE(40)
         LF_BWD_CASE(48) LF_BWD_CASE(52) LF_BWD_CASE(56) LF_BWD_CASE(64)

@@ -14,13 +14,23 @@
 namespace laplace {
 namespace {
 
+// Messages are assembled with std::to_string: inserting numbers into a
+// std::ostream (which TORCH_CHECK does for non-string arguments) crashes at
+// call time in extensions built in this image (torch 2.11, GCC 13).
+std::string num(int64_t v) { return std::to_string(v); }
+std::string shape_str(at::IntArrayRef s) {
+    std::string r = "[";
+    for (size_t i = 0; i < s.size(); ++i) r += (i ? ", " : "") + std::to_string(s[i]);
+    return r + "]";
+}
+
 int dtype_code(const at::Tensor& t) {
     switch (t.scalar_type()) {
         case at::kFloat: return LF_F32;
         case at::kDouble: return LF_F64;
         case at::kHalf: return LF_F16;
         case at::kBFloat16: return LF_BF16;
-        default: TORCH_CHECK(false, "unsupported dtype ", t.scalar_type());
+        default: TORCH_CHECK(false, std::string("unsupported dtype ") + c10::toString(t.scalar_type()));
     }
     return -1;
 }
@@ -30,17 +40,17 @@ lf_stream_t stream_of(const at::Tensor& t) {
 }
 
 void raise_on(int rc, const char* op) {
-    TORCH_CHECK(rc == LF_OK, op, " failed (code ", rc, "): ", lf_last_error());
+    TORCH_CHECK(rc == LF_OK, std::string(op) + " failed (code " + num(rc) + "): " + lf_last_error());
 }
 
 // Reference shape_check (src/LaplaceSubtraction_cuda.cu:12-28).
 void shape_check(const at::Tensor& query, const at::Tensor& key) {
     TORCH_CHECK(query.ndimension() == 4,
-                "4D weight tensor (batch size, head number, sequence length, channel) expected, but got: ",
-                query.ndimension());
+                "4D weight tensor (batch size, head number, sequence length, channel) expected, but got: " +
+                    num(query.ndimension()));
     TORCH_CHECK(key.ndimension() == 4,
-                "4D weight tensor (batch size, head number, sequence length, channel) expected, but got: ",
-                key.ndimension());
+                "4D weight tensor (batch size, head number, sequence length, channel) expected, but got: " +
+                    num(key.ndimension()));
     TORCH_CHECK(query.is_contiguous(), "query tensor has to be contiguous");
     TORCH_CHECK(key.is_contiguous(), "key tensor has to be contiguous");
     TORCH_CHECK(query.size(0) == key.size(0) && query.size(1) == key.size(1) && query.size(3) == key.size(2),
@@ -50,10 +60,10 @@ void shape_check(const at::Tensor& query, const at::Tensor& key) {
 }
 
 void out_check(const at::Tensor& t, const at::Tensor& like, at::IntArrayRef sizes, const char* name) {
-    TORCH_CHECK(t.is_cuda() && t.device() == like.device(), name, " must be on the query's device");
-    TORCH_CHECK(t.is_contiguous(), name, " has to be contiguous");
-    TORCH_CHECK(t.scalar_type() == like.scalar_type(), name, " must have the query's dtype");
-    TORCH_CHECK(t.sizes() == sizes, name, " has shape ", t.sizes(), ", expected ", sizes);
+    TORCH_CHECK(t.is_cuda() && t.device() == like.device(), std::string(name) + " must be on the query's device");
+    TORCH_CHECK(t.is_contiguous(), std::string(name) + " has to be contiguous");
+    TORCH_CHECK(t.scalar_type() == like.scalar_type(), std::string(name) + " must have the query's dtype");
+    TORCH_CHECK(t.sizes() == sizes, std::string(name) + " has shape " + shape_str(t.sizes()) + ", expected " + shape_str(sizes));
 }
 
 struct Dims {
@@ -137,7 +147,7 @@ static void ns_checks(const at::Tensor& mat, const at::Tensor& output) {
     TORCH_CHECK(output.is_cuda() && output.device() == mat.device(), "output must be on mat's device");
     TORCH_CHECK(output.scalar_type() == mat.scalar_type(), "output must have mat's dtype");
     const int64_t N = mat.size(2);
-    TORCH_CHECK(NewtonInverse_supports((int)N), "NewtonInverse: N=", N,
+    TORCH_CHECK(NewtonInverse_supports((int)N), "NewtonInverse: N=" + num(N) +
                 " is not supported on this device (insufficient smem or out of range)");
 }
 
@@ -165,7 +175,7 @@ void NewtonInverse_backward_cuda(const at::Tensor grad_output, const at::Tensor 
     TORCH_CHECK(grad_mat.is_cuda() && grad_mat.device() == inverse.device(), "grad_mat must be on inverse's device");
     const int64_t N = inverse.size(2);
     TORCH_CHECK(inverse.size(3) == N, "last two dims must be equal");
-    TORCH_CHECK(NewtonInverse_supports((int)N), "NewtonInverse: N=", N,
+    TORCH_CHECK(NewtonInverse_supports((int)N), "NewtonInverse: N=" + num(N) +
                 " is not supported on this device (insufficient smem or out of range)");
     raise_on(lf_newton_inverse_bwd(grad_output.data_ptr(), inverse.data_ptr(), grad_mat.data_ptr(),
                                    inverse.size(0) * inverse.size(1), N, dtype_code(inverse), stream_of(inverse)),

@@ -219,6 +219,8 @@ def test_extension_ops_match_capi(cuda, ext):
         ext.LaplaceSubtraction_forward(q, k[:, :, :5].contiguous(), s)
     with pytest.raises(RuntimeError, match="contiguous"):
         ext.LaplaceSubtraction_forward(q.transpose(2, 3), k, s)
+    with pytest.raises(RuntimeError, match=r"output has shape \[2, 2, 70, 48\]"):
+        ext.LaplaceSubtraction_forward(q, k, s[..., :48].contiguous())
 
 
 def test_autograd_function(cuda):
