@@ -549,6 +549,213 @@ lsub_bwd_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* __res
     cluster.sync();  // keep this CTA's shared memory alive until peers are done
 }
 
+// Fast path of the fused backward for d <= 32 and m <= 64 (one channel
+// block, one landmark chunk per warp): the pyramid-ViT shapes.  Staging maps
+// four threads to each of the 64 rows of a chunk (thread (r, q) owns the
+// landmark quarter q and channel octet q of row r), so row sums are two
+// shuffles, column sums stay in registers for the whole CTA, and the next
+// chunk's dS and Q are loaded into registers while the current one is being
+// consumed.  Same arithmetic and cluster reduction as lsub_bwd_kernel.
+template <typename T, int MB, bool DQ, bool DK>
+__global__ void __launch_bounds__(kThreads, 1)
+lsub_bwd_fast_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* __restrict__ kT,
+                     T* __restrict__ dq, T* __restrict__ dk, BwdGeom geo) {
+    using A = typename Elem<T>::acc;
+    constexpr int RC = kRowChunk;   // 64 rows per chunk
+    constexpr int CPT = MB / 4;     // landmarks per staging thread
+    constexpr int CW = 32;          // channels (one block)
+    constexpr int MP = MB;          // staged row stride
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int n = geo.n, m = geo.m, d = geo.d;
+    A* gs = reinterpret_cast<A*>(smem_raw);  // [RC][MP]  dS (not doubled)
+    A* qs = gs + RC * MP;                      // [RC][CW]
+    A* rsum = qs + RC * CW;                    // [RC]
+    A* csum = rsum + RC;                       // [MP]
+    A* dkb = csum + MP;                        // [CW][KSTR]
+    A* cpart = dkb + CW * geo.KSTR;            // [8][MP]
+
+    cg::cluster_group cluster = cg::this_cluster();
+    const int bh = blockIdx.y;
+    const int split = blockIdx.x;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int c = lane;                 // this lane's channel
+    const bool lane_active = c < d;
+    const int rg = warp;                // row group (8 warps)
+    const int sr = tid >> 2, sq = tid & 3;
+
+    const T* Gb = g + (int64_t)bh * n * m;
+    const T* Qb = q + (int64_t)bh * n * d;
+    const T* Kb = kT + (int64_t)bh * d * m;
+
+    A kreg[MB];
+    A dka[MB];
+#pragma unroll
+    for (int jj = 0; jj < MB; ++jj) {
+        kreg[jj] = (lane_active && jj < m) ? Elem<T>::load(Kb[(int64_t)c * m + jj]) : A(0);
+        dka[jj] = A(0);
+    }
+    A colp[CPT];
+#pragma unroll
+    for (int k = 0; k < CPT; ++k) colp[k] = A(0);
+
+    const int64_t r_begin = (int64_t)split * geo.rows_per_cta;
+    const int64_t r_end = (r_begin + geo.rows_per_cta < (int64_t)n) ? r_begin + geo.rows_per_cta : (int64_t)n;
+
+    A pg[CPT], pq[8];
+    auto load_chunk = [&](int64_t rc) {
+        const int64_t row = rc + sr;
+        const bool ok = row < r_end;
+        const T* grow = Gb + row * m + sq * CPT;
+#pragma unroll
+        for (int k = 0; k < CPT; ++k) pg[k] = (ok && sq * CPT + k < m) ? Elem<T>::load(grow[k]) : A(0);
+        const T* qrow = Qb + row * d + sq * 8;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) pq[k] = (ok && sq * 8 + k < d) ? Elem<T>::load(qrow[k]) : A(0);
+    };
+    if (r_begin < r_end) load_chunk(r_begin);
+
+    for (int64_t rc = r_begin; rc < r_end; rc += RC) {
+        const int rows = (int)((r_end - rc) < RC ? (r_end - rc) : RC);
+        __syncthreads();  // previous chunk fully consumed
+        {
+            A rs = A(0);
+#pragma unroll
+            for (int k = 0; k < CPT; ++k) {
+                gs[sr * MP + sq * CPT + k] = pg[k];
+                rs += pg[k];
+                if (DK) colp[k] += pg[k];
+            }
+            rs += __shfl_xor_sync(0xffffffffu, rs, 1);
+            rs += __shfl_xor_sync(0xffffffffu, rs, 2);
+            if (sq == 0) rsum[sr] = rs;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) qs[sr * CW + sq * 8 + k] = pq[k];
+        }
+        __syncthreads();
+        if (rc + RC < r_end) load_chunk(rc + RC);  // in flight during the compute below
+
+        if (lane_active) {
+#pragma unroll 1
+            for (int i = rg; i < rows; i += kThreads / 32) {
+                const A qv = qs[i * CW + c];
+                const A* grow = gs + i * MP;
+                A dqa = A(0);
+#pragma unroll
+                for (int j4 = 0; j4 < MB; j4 += 4) {
+                    A gv[4];
+                    if constexpr (sizeof(A) == 4) {
+                        float4 t4 = *reinterpret_cast<const float4*>(grow + j4);
+                        gv[0] = t4.x; gv[1] = t4.y; gv[2] = t4.z; gv[3] = t4.w;
+                        bwd_quad<DQ, DK>(qv, kreg[j4], kreg[j4 + 1], kreg[j4 + 2], kreg[j4 + 3], gv, dqa,
+                                         dka[j4], dka[j4 + 1], dka[j4 + 2], dka[j4 + 3]);
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            gv[e] = grow[j4 + e];
+                            const A t = step_of<A>(qv, kreg[j4 + e]);
+                            if (DQ) dqa = fma_acc(gv[e], t, dqa);
+                            if (DK) dka[j4 + e] = fma_acc(gv[e], t, dka[j4 + e]);
+                        }
+                    }
+                }
+                // sum_j g*t was accumulated with g (not 2g): dQ = 2*acc - sum_j g
+                if (DQ) dq[((int64_t)bh * n + rc + i) * d + c] = Elem<T>::store(A(2) * dqa - rsum[i]);
+            }
+        }
+    }
+
+    if (!DK) return;
+
+    // Column sums: reduce colp over the 8 rows of the warp that share a
+    // quarter (lanes 4 apart), then across warps through shared memory.
+#pragma unroll
+    for (int k = 0; k < CPT; ++k) {
+        A v = colp[k];
+        v += __shfl_xor_sync(0xffffffffu, v, 4);
+        v += __shfl_xor_sync(0xffffffffu, v, 8);
+        v += __shfl_xor_sync(0xffffffffu, v, 16);
+        if (lane < 4) cpart[warp * MP + sq * CPT + k] = v;
+    }
+    for (int e = tid; e < CW * geo.KSTR; e += kThreads) dkb[e] = A(0);
+    __syncthreads();
+    for (int j = tid; j < m; j += kThreads) {
+        A sacc = A(0);
+        for (int w = 0; w < kThreads / 32; ++w) sacc += cpart[w * MP + j];
+        csum[j] = sacc;
+    }
+    if (lane_active) {
+#pragma unroll
+        for (int jj = 0; jj < MB; ++jj)
+            if (jj < m) atomicAdd(&dkb[c * geo.KSTR + jj], A(-2) * dka[jj]);
+    }
+    __syncthreads();
+    for (int e = tid; e < d * m; e += kThreads) {
+        int cc = e / m, j = e - cc * m;
+        dkb[cc * geo.KSTR + j] += csum[j];
+    }
+    cluster.sync();
+    const int cs = (int)cluster.num_blocks();
+    const int rank = (int)cluster.block_rank();
+    const int total = d * m;
+    const int per = (total + cs - 1) / cs;
+    const int e0 = rank * per, e1 = min(total, e0 + per);
+    T* dkout = dk + (int64_t)bh * d * m;
+    for (int e = e0 + tid; e < e1; e += kThreads) {
+        int cc = e / m, j = e - cc * m;
+        A sacc = A(0);
+        for (int r = 0; r < cs; ++r) {
+            const A* peer = cluster.map_shared_rank(dkb, r);
+            sacc += peer[cc * geo.KSTR + j];
+        }
+        dkout[e] = Elem<T>::store(sacc);
+    }
+    cluster.sync();
+}
+
+template <typename T, int MB, bool DQ, bool DK>
+int launch_bwd_fast(const T* g, const T* q, const T* kT, T* dq, T* dk, int64_t bh, int64_t n, int64_t m,
+                    int64_t d, cudaStream_t st) {
+    using A = typename Elem<T>::acc;
+    BwdGeom geo;
+    geo.n = (int)n; geo.m = (int)m; geo.d = (int)d;
+    geo.DBC = 1; geo.MCN = 1; geo.RG = kThreads / 32; geo.MP = MB; geo.RC = kRowChunk;
+    geo.KSTR = (int)(m | 1);
+    size_t smem = sizeof(A) * ((size_t)kRowChunk * MB + (size_t)kRowChunk * 32 + kRowChunk + MB +
+                               (size_t)32 * geo.KSTR + (size_t)(kThreads / 32) * MB);
+    auto kern = lsub_bwd_fast_kernel<T, MB, DQ, DK>;
+    if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    const int64_t slots = cta_slots(kern, smem);
+    const int64_t max_by_rows = (n + kRowChunk - 1) / kRowChunk;
+    int64_t cs = 1;
+    double best = -1.0;
+    for (int64_t c = 1; c <= 8 && c <= (max_by_rows < 1 ? 1 : max_by_rows); ++c) {
+        double eff = wave_efficiency(bh * c, slots);
+        if (eff > best + 1e-9) { best = eff; cs = c; }
+    }
+    int64_t rpc = (n + cs - 1) / cs;
+    rpc = ((rpc + kRowChunk - 1) / kRowChunk) * kRowChunk;
+    geo.rows_per_cta = (int)rpc;
+    if (bh > 65535) { set_error("b*h = %lld exceeds 65535", (long long)bh); return LF_ERR_UNSUPPORTED; }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)cs, (unsigned)bh, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)cs;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t err = cudaLaunchKernelEx(&cfg, kern, g, q, kT, dq, dk, geo);
+    if (err != cudaSuccess) {
+        set_error("lsub_bwd_fast_kernel launch: %s", cudaGetErrorString(err));
+        return LF_ERR_CUDA;
+    }
+    return check_launch("lsub_bwd_fast_kernel");
+}
+
 // Landmark chunk per warp (MB) and number of chunks (mcn): least padding of m
 // with at most 8 chunks; ties prefer chunks of at most 52 landmarks (larger
 // ones spill registers in the fused kernel), then the larger chunk.
@@ -647,6 +854,20 @@ int launch_bwd_t(const void* g, const void* q, const void* kT, void* dq, void* d
     const T* K = static_cast<const T*>(kT);
     T* DQp = static_cast<T*>(dq);
     T* DKp = static_cast<T*>(dk);
+    if constexpr (sizeof(T) != 8) {
+        // fast path: one channel block, one landmark chunk of 4..64 (multiple of 4)
+        if (d <= 32 && m <= 64) {
+            const int64_t m4 = (m + 3) & ~3;
+            switch (m4 <= 16 ? 16 : (m4 <= 32 ? 32 : (m4 <= 48 ? 48 : (m4 <= 52 ? 52 : (m4 <= 56 ? 56 : 64))))) {
+                case 16: return launch_bwd_fast<T, 16, DQ, DK>(G, Q, K, DQp, DKp, bh, n, m, d, st);
+                case 32: return launch_bwd_fast<T, 32, DQ, DK>(G, Q, K, DQp, DKp, bh, n, m, d, st);
+                case 48: return launch_bwd_fast<T, 48, DQ, DK>(G, Q, K, DQp, DKp, bh, n, m, d, st);
+                case 52: return launch_bwd_fast<T, 52, DQ, DK>(G, Q, K, DQp, DKp, bh, n, m, d, st);
+                case 56: return launch_bwd_fast<T, 56, DQ, DK>(G, Q, K, DQp, DKp, bh, n, m, d, st);
+                default: return launch_bwd_fast<T, 64, DQ, DK>(G, Q, K, DQp, DKp, bh, n, m, d, st);
+            }
+        }
+    }
     int mcn = 1;
     int mb = pick_mb(m, mcn);
     if (mb == 0) {
