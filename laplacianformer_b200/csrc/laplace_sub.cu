@@ -874,15 +874,9 @@ int launch_bwd_t(const void* g, const void* q, const void* kT, void* dq, void* d
         set_error("LaplaceSubtraction backward supports m <= 512 (got %lld)", (long long)m);
         return LF_ERR_UNSUPPORTED;
     }
-    static const int minb_env = [] {
-        const char* e = getenv("LFB_BWD_MINB");
-        return e ? atoi(e) : 2;
-    }();
     constexpr int kMinb = (DQ && sizeof(T) != 8) ? 2 : 1;
 #define LF_BWD_CASE(MBV)                                                                              \
     case MBV:                                                                                         \
-        if (kMinb == 2 && minb_env == 1)                                                              \
-            return launch_bwd_mb<T, MBV, DQ, DK, 1>(G, Q, K, DQp, DKp, bh, n, m, d, mcn, st);          \
         return launch_bwd_mb<T, MBV, DQ, DK, kMinb>(G, Q, K, DQp, DKp, bh, n, m, d, mcn, st);
     switch (mb) {
         LF_BWD_CASE(8) LF_BWD_CASE(16) LF_BWD_CASE(24) LF_BWD_CASE(32) LF_BWD_CASE(40)
