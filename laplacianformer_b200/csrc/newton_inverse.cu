@@ -181,18 +181,19 @@ __device__ __forceinline__ float split_scale(float mx) {
 
 __device__ __forceinline__ void split_store(unsigned char* hi_base, unsigned char* lo_base, int r,
                                             int col0, const float (&v)[32], float s) {
-    // v holds columns [col0, col0+32) of row r; col0 is a multiple of 32.
+    // v holds columns [col0, col0+32) of row r (col0 a multiple of 32); stores
+    // hi = fp16(v*s) and lo = fp16(v*s - hi), two elements per conversion.
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
         uint32_t h[4], l[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-            float x0 = v[8 * k + 2 * e] * s, x1 = v[8 * k + 2 * e + 1] * s;
-            __half h0 = __float2half_rn(x0), h1 = __float2half_rn(x1);
-            __half l0 = __float2half_rn(x0 - __half2float(h0));
-            __half l1 = __float2half_rn(x1 - __half2float(h1));
-            h[e] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
-            l[e] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
+            const float2 xs = make_float2(v[8 * k + 2 * e] * s, v[8 * k + 2 * e + 1] * s);
+            const __half2 hh = __float22half2_rn(xs);
+            const float2 hb = __half22float2(hh);
+            const __half2 ll = __float22half2_rn(make_float2(xs.x - hb.x, xs.y - hb.y));
+            h[e] = *reinterpret_cast<const uint32_t*>(&hh);
+            l[e] = *reinterpret_cast<const uint32_t*>(&ll);
         }
         uint32_t off = op_chunk_offset(r, (col0 >> 3) + k);
         *reinterpret_cast<uint4*>(hi_base + off) = make_uint4(h[0], h[1], h[2], h[3]);
@@ -395,10 +396,8 @@ ns_tc_fwd_kernel(const T* __restrict__ a, T* __restrict__ x, int n, int iters, i
             tmem_ld32(t_w + col0, wv);
             tmem_wait_ld();
             reg_fence(wv);
-            const float iv = 1.f / sV, ip = 1.f / sP;
-#pragma unroll
-            for (int e = 0; e < 32; ++e) wv[e] = wv[e] * iv * ip;
-            split_store(Wh, Wl, row, col0, wv, sW);
+            // acc = W * sV * sP; the stored operand is W * sW (all powers of two)
+            split_store(Wh, Wl, row, col0, wv, sW * (1.f / sV) * (1.f / sP));
         }
         fence_async_smem();
         tc_fence_before();
@@ -436,10 +435,10 @@ ns_tc_fwd_kernel(const T* __restrict__ a, T* __restrict__ x, int n, int iters, i
             tmem_wait_ld();
             reg_fence(yv);
             reg_fence(vn);
-            const float iw = 1.f / sW, iv = 1.f / sV;
+            const float c2 = (1.f / sW) * (1.f / sV);  // acc = Y * sW * sV
 #pragma unroll
             for (int e = 0; e < 32; ++e) {
-                vn[e] = fmaf(2.f, vn[e], -(yv[e] * iw * iv));
+                vn[e] = fmaf(yv[e], -c2, 2.f * vn[e]);
                 lmax = fmaxf(lmax, fabsf(vn[e]));
                 lsum += fabsf(vn[e]);
             }
