@@ -293,7 +293,28 @@ int launch_fwd(const void* q, const void* kT, void* s, int64_t bh, int64_t n, in
         return launch_fwd_dr<T, 16>(Q, K, S, bh, n, m, d, st);
     } else {
         if (d <= 16) return launch_fwd_dr<T, 16>(Q, K, S, bh, n, m, d, st);
-        if (d <= 32) return launch_fwd_dr<T, 32>(Q, K, S, bh, n, m, d, st);
+        if (d <= 32) {
+            static const int variant = [] { const char* e = getenv("LFB_FWD_VARIANT"); return e ? atoi(e) : 0; }();
+            if (variant == 4) {
+                switch (pick_mc(m)) {
+                    case 4: return launch_fwd_mc<T, 4, 4, 16>(Q, K, S, bh, n, m, d, st);
+                    case 5: return launch_fwd_mc<T, 4, 5, 16>(Q, K, S, bh, n, m, d, st);
+                    case 6: return launch_fwd_mc<T, 4, 6, 16>(Q, K, S, bh, n, m, d, st);
+                    case 7: return launch_fwd_mc<T, 4, 7, 16>(Q, K, S, bh, n, m, d, st);
+                    default: return launch_fwd_mc<T, 4, 8, 16>(Q, K, S, bh, n, m, d, st);
+                }
+            }
+            if (variant == 2) {
+                switch (pick_mc(m)) {
+                    case 4: return launch_fwd_mc<T, 2, 4, 16>(Q, K, S, bh, n, m, d, st);
+                    case 5: return launch_fwd_mc<T, 2, 5, 16>(Q, K, S, bh, n, m, d, st);
+                    case 6: return launch_fwd_mc<T, 2, 6, 16>(Q, K, S, bh, n, m, d, st);
+                    case 7: return launch_fwd_mc<T, 2, 7, 16>(Q, K, S, bh, n, m, d, st);
+                    default: return launch_fwd_mc<T, 2, 8, 16>(Q, K, S, bh, n, m, d, st);
+                }
+            }
+            return launch_fwd_dr<T, 32>(Q, K, S, bh, n, m, d, st);
+        }
         if (d <= 64) return launch_fwd_dr<T, 64>(Q, K, S, bh, n, m, d, st);
         return launch_fwd_dr<T, 32>(Q, K, S, bh, n, m, d, st);
     }

@@ -38,11 +38,27 @@ namespace lfb {
 // whose bounded wait expired.  Read and cleared by lf_device_status().
 __device__ int g_ns_status = 0;
 
+// Phase timestamps of CTA 0 for kernel development builds (-DLF_NS_TRACE);
+// compiled out otherwise.
+#ifdef LF_NS_TRACE
+__device__ long long g_ns_trace[16][32];
+#define NS_TRACE(it, k)                                                                          \
+    do {                                                                                         \
+        if (blockIdx.x == 0 && (threadIdx.x == 0 || threadIdx.x == 256) && (it) < 16)            \
+            g_ns_trace[it][(k) + (threadIdx.x ? 16 : 0)] = clock64();                            \
+    } while (0)
+#else
+#define NS_TRACE(it, k) \
+    do {                \
+    } while (0)
+#endif
+
 namespace {
 
 constexpr int kNsThreads = 512;
 constexpr int kTile = 128;                 // padded matrix size
 constexpr int kOpBytes = kTile * kTile * 2; // one fp16 operand (32 KB)
+constexpr bool kSplitW = false;        // W = V P as two N = 64 halves (true) or one N = 128 product
 constexpr int kTmemCols = 512;             // W and Y accumulators + fp32 V (384 used)
 
 // ---------------------------------------------------------------------------
@@ -212,8 +228,6 @@ struct NsShared {
     uint64_t bar[3];            // W columns [0,64), W columns [64,128), Y
     uint32_t tmem_base;
     float red[kNsThreads / 32][4];
-    float rowpart[4][kTile];    // per column-group partial row sums of |V|
-    float rmax[4];              // per lane-quadrant max of the row sums
     float colsum[kTile];
 };
 
@@ -268,7 +282,9 @@ __device__ __forceinline__ int stage_idx(int i, int c) { return i * kTile + (c ^
 //      + W[:, 64:128] V[64:128,:] issued when groups 2,3 have     -> bar[2]
 //   V <- 2V - Y (all warps), new split scale from a block max.
 // W's split scale comes from the bound max|W| <= ||V||_inf * max|P| (known
-// before the product), so its conversion needs no reduction.
+// before the product; ||V||_inf exactly for V0, then n * max|V|), so its
+// conversion needs no reduction.  A loose bound only lowers the magnitude of
+// the scaled values; fp16 keeps 11 significant bits down to 2^-14.
 template <typename T>
 __global__ void __launch_bounds__(kNsThreads, 1)
 ns_tc_fwd_kernel(const T* __restrict__ a, T* __restrict__ x, int n, int iters, int mode, float reg,
@@ -380,25 +396,38 @@ ns_tc_fwd_kernel(const T* __restrict__ a, T* __restrict__ x, int n, int iters, i
         const int nterm = (precision == LF_NS_PREC_MIXED && it < iters - 2) ? 1 : 3;
         const bool last = (it == iters - 1);
         const float sW = split_scale(vinf * pmax);
+        NS_TRACE(it, 0);
         // ---- W = V P in two column halves ---------------------------------
         if (tid == 0) {
             tc_fence_after();
-            issue_mma<64>(tmem, aVh, aVl, aPh, aPl, 0, kTile / 16, nterm, true);
-            mma_commit(&sh.bar[0]);
-            issue_mma<64>(tmem + 64, aVh, aVl, aPh + 16384, aPl + 16384, 0, kTile / 16, nterm, true);
-            mma_commit(&sh.bar[1]);
+            if (kSplitW) {
+                issue_mma<64>(tmem, aVh, aVl, aPh, aPl, 0, kTile / 16, nterm, true);
+                mma_commit(&sh.bar[0]);
+                issue_mma<64>(tmem + 64, aVh, aVl, aPh + 16384, aPl + 16384, 0, kTile / 16, nterm, true);
+                mma_commit(&sh.bar[1]);
+            } else {
+                // one N = 128 product reads each A tile once (M = 128 MMAs with
+                // both operands in shared memory are bound by its bandwidth)
+                issue_mma<128>(tmem, aVh, aVl, aPh, aPl, 0, kTile / 16, nterm, true);
+                mma_commit(&sh.bar[0]);
+                mma_commit(&sh.bar[1]);
+            }
         }
+        NS_TRACE(it, 1);
         const bool lo_half = cg < 2;
         bool okw = mbar_wait(&sh.bar[lo_half ? 0 : 1], phase);
+        NS_TRACE(it, 2);
         tc_fence_after();
         {
             float wv[32];
             tmem_ld32(t_w + col0, wv);
             tmem_wait_ld();
             reg_fence(wv);
+            NS_TRACE(it, 12);
             // acc = W * sV * sP; the stored operand is W * sW (all powers of two)
             split_store(Wh, Wl, row, col0, wv, sW * (1.f / sV) * (1.f / sP));
         }
+        NS_TRACE(it, 3);
         fence_async_smem();
         tc_fence_before();
         // ---- Y = W V, K split so that the first half starts early ----------
@@ -420,14 +449,16 @@ ns_tc_fwd_kernel(const T* __restrict__ a, T* __restrict__ x, int n, int iters, i
         } else {
             named_arrive(2, kNsThreads / 2 + 32);
         }
+        NS_TRACE(it, 4);
         okw = mbar_wait(&sh.bar[2], phase) && okw;
+        NS_TRACE(it, 5);
         phase ^= 1;
         ok = !__syncthreads_or(!okw);
         if (!ok) break;
         tc_fence_after();
         // ---- V <- 2V - Y ----------------------------------------------------
         float vn[32];
-        float lmax = 0.f, lsum = 0.f;
+        float lmax = 0.f;
         {
             float yv[32];
             tmem_ld32(t_y + col0, yv);
@@ -435,12 +466,12 @@ ns_tc_fwd_kernel(const T* __restrict__ a, T* __restrict__ x, int n, int iters, i
             tmem_wait_ld();
             reg_fence(yv);
             reg_fence(vn);
+            NS_TRACE(it, 9);
             const float c2 = (1.f / sW) * (1.f / sV);  // acc = Y * sW * sV
 #pragma unroll
             for (int e = 0; e < 32; ++e) {
                 vn[e] = fmaf(yv[e], -c2, 2.f * vn[e]);
                 lmax = fmaxf(lmax, fabsf(vn[e]));
-                lsum += fabsf(vn[e]);
             }
         }
         if (last) {
@@ -451,27 +482,24 @@ ns_tc_fwd_kernel(const T* __restrict__ a, T* __restrict__ x, int n, int iters, i
             }
             break;
         }
+        NS_TRACE(it, 10);
         tmem_st32(t_v + col0, vn);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) lmax = fmaxf(lmax, __shfl_xor_sync(0xffffffffu, lmax, o));
         if (lane == 0) sh.red[warp][0] = lmax;
-        sh.rowpart[cg][row] = lsum;
         __syncthreads();
+        NS_TRACE(it, 11);
         float m = sh.red[0][0];
         for (int w = 1; w < kNsThreads / 32; ++w) m = fmaxf(m, sh.red[w][0]);
         sV = split_scale(m);
-        if (cg == 0) {
-            float rs = sh.rowpart[0][row] + sh.rowpart[1][row] + sh.rowpart[2][row] + sh.rowpart[3][row];
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) rs = fmaxf(rs, __shfl_xor_sync(0xffffffffu, rs, o));
-            if (lane == 0) sh.rmax[quad] = rs;
-        }
+        vinf = (float)n * m;  // ||V||_inf <= n * max|V|
         split_store(Vh, Vl, row, col0, vn, sV);
+        NS_TRACE(it, 7);
         tmem_wait_st();
         fence_async_smem();
         tc_fence_before();
         __syncthreads();
-        vinf = fmaxf(fmaxf(sh.rmax[0], sh.rmax[1]), fmaxf(sh.rmax[2], sh.rmax[3]));
+        NS_TRACE(it, 8);
     }
     if (!ok && tid == 0) atomicExch(&g_ns_status, (int)LF_ERR_TIMEOUT);
     tc_fence_before();
@@ -818,3 +846,9 @@ extern "C" int lf_device_status(int clear) {
     }
     return v;
 }
+
+#ifdef LF_NS_TRACE
+extern "C" LF_API int lf_ns_trace_read(long long* out) {
+    return cudaMemcpyFromSymbol(out, g_ns_trace, sizeof(long long) * 16 * 32) == cudaSuccess ? 0 : 1;
+}
+#endif
