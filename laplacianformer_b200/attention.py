@@ -1,0 +1,70 @@
+"""Laplacian-kernel linear attention block built from the two operators.
+
+The reference ships only the operators; the paper's attention composes them
+as follows (configuration 4 of the benchmark):
+
+    L      = pool(K)                                  landmarks [B,H,M,D]
+    K_QL   = exp(-LaplaceSub(Q, L^T) / sigma)          [B,H,N,M]
+    K_LK   = exp(-LaplaceSub(L, K^T) / sigma)          [B,H,M,N]
+    X      = NewtonInverse(exp(-LaplaceSub(L, L^T) / sigma), iters)   [B,H,M,M]
+    out    = K_QL @ X @ (K_LK @ V)                     [B,H,N,D]
+
+Every L1 distance and the inverse run on the B200 kernels (through the
+autograd functions of :mod:`laplacianformer_b200.ops`); the exponentials and
+the small products are PyTorch ops.  The landmark kernel matrix and its
+inverse are kept in fp32 whatever the storage type of Q/K/V.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from .ops import INIT_REFERENCE, PREC_SPLIT3, laplace_subtraction, newton_inverse
+
+
+def pool_landmarks(k: torch.Tensor, grid: int, pool: int) -> torch.Tensor:
+    """Average-pool keys laid out on a grid x grid token grid: [B,H,grid^2,D] -> [B,H,(grid/pool)^2,D]."""
+    B, H, N, D = k.shape
+    assert N == grid * grid and grid % pool == 0
+    s = grid // pool
+    g = k.view(B, H, s, pool, s, pool, D).mean((3, 5))
+    return g.reshape(B, H, s * s, D)
+
+
+def laplacian_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, landmarks: torch.Tensor,
+                        iters: int = 8, sigma: float | None = None, init_mode: int = INIT_REFERENCE,
+                        precision: int = PREC_SPLIT3) -> torch.Tensor:
+    """out = exp(-S_QL/sigma) X exp(-S_LK/sigma) V, X the Newton–Schulz inverse of exp(-S_LL/sigma)."""
+    D = q.shape[-1]
+    sigma = math.sqrt(D) if sigma is None else sigma
+    L = landmarks
+    s_ql = laplace_subtraction(q, L.transpose(-1, -2).contiguous())          # [B,H,N,M]
+    s_lk = laplace_subtraction(L, k.transpose(-1, -2).contiguous())          # [B,H,M,N]
+    Lf = L.float()
+    s_ll = laplace_subtraction(Lf, Lf.transpose(-1, -2).contiguous())        # [B,H,M,M] fp32
+    k_ql = torch.exp(-s_ql / sigma)
+    k_lk = torch.exp(-s_lk / sigma)
+    x = newton_inverse(torch.exp(-s_ll / sigma), iters, init_mode=init_mode, precision=precision)
+    kv = k_lk @ v                                                            # [B,H,M,D]
+    return k_ql @ (x.to(q.dtype) @ kv)
+
+
+class LaplacianAttention(torch.nn.Module):
+    """Multi-head Laplacian linear attention over a square token grid."""
+
+    def __init__(self, dim: int, heads: int, grid: int, pool: int = 2, iters: int = 8, sigma: float | None = None):
+        super().__init__()
+        assert dim % heads == 0
+        self.heads, self.grid, self.pool, self.iters = heads, grid, pool, iters
+        self.sigma = sigma
+        self.qkv = torch.nn.Linear(dim, 3 * dim)
+        self.proj = torch.nn.Linear(dim, dim)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        B, N, C = x.shape
+        h = self.heads
+        q, k, v = self.qkv(x).view(B, N, 3, h, C // h).permute(2, 0, 3, 1, 4).contiguous().unbind(0)
+        L = pool_landmarks(k, self.grid, self.pool)
+        out = laplacian_attention(q.contiguous(), k.contiguous(), v.contiguous(), L.contiguous(), self.iters, self.sigma)
+        return self.proj(out.transpose(1, 2).reshape(B, N, C))

@@ -30,7 +30,11 @@
 // CUDA-core path: fp64 inputs, the LF_NS_PREC_FP32_SIMT mode, the backward
 // and the residual use row-blocked fp32/fp64 FMA loops with V resident in
 // shared memory.
+#include <cooperative_groups.h>
+
 #include "lf_common.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace lfb {
 
@@ -688,6 +692,169 @@ ns_residual_kernel(const T* __restrict__ a, const T* __restrict__ x, Acc* __rest
     }
 }
 
+// ---------------------------------------------------------------------------
+// Matrices with 128 < n <= 256 (fp32), CUDA cores.
+// ---------------------------------------------------------------------------
+constexpr int kMaxN = 256;
+constexpr int kBigThreads = 512;
+
+// A cluster of two CTAs per matrix; CTA r of the pair owns rows
+// [r*h, min(n, (r+1)*h)), h = ceil(n/2).  The current iterate V lives in the
+// output buffer (global memory, L2-resident) and the CTA's rows of the next
+// iterate in shared memory; once both halves are complete (cluster barrier)
+// they are written back.  W = V P and Y = W V are formed 16 rows at a time:
+// the reference 2-buffer association (V P) V.
+__global__ void __launch_bounds__(kBigThreads, 1)
+ns_simt_big_kernel(const float* __restrict__ a, float* __restrict__ x, int n, int iters, int mode, float reg) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    cg::cluster_group cluster = cg::this_cluster();
+    const int S = n + 1;
+    const int h = (n + 1) / 2;
+    float* Vn = reinterpret_cast<float*>(smem_raw);  // [h][S]
+    float* Wr = Vn + (size_t)h * S;                   // [kRB][S]
+    float* red = Wr + kRB * S;                        // [kBigThreads/32]
+    const int tid = threadIdx.x;
+    const int rank = (int)cluster.block_rank();
+    const int64_t mat = blockIdx.x / 2;
+    const float* A = a + mat * (int64_t)n * n;
+    float* X = x + mat * (int64_t)n * n;
+    const int r_lo = rank * h, r_hi = min(n, r_lo + h);
+    auto P = [&](int i, int j) -> float { return A[(int64_t)i * n + j] + (i == j ? reg : 0.f); };
+
+    float c0;
+    if (mode == LF_NS_INIT_REFERENCE) {
+        float mx = -1e30f;
+        for (int i = tid; i < n; i += kBigThreads) {
+            float s = 0.f;
+            for (int j = 0; j < n; ++j) s += P(i, j);
+            mx = fmaxf(mx, s);
+        }
+        mx = block_reduce_max<float>(mx, red);
+        c0 = __fdiv_rn(1.8f, mx * mx);
+    } else {
+        float r1 = 0.f, ri = 0.f;
+        for (int i = tid; i < n; i += kBigThreads) {
+            float rs = 0.f, cs = 0.f;
+            for (int j = 0; j < n; ++j) { rs += fabsf(P(i, j)); cs += fabsf(P(j, i)); }
+            ri = fmaxf(ri, rs);
+            r1 = fmaxf(r1, cs);
+        }
+        ri = block_reduce_max<float>(ri, red);
+        r1 = block_reduce_max<float>(r1, red);
+        c0 = __fdiv_rn(1.f, r1 * ri);
+    }
+    for (int e = tid; e < (r_hi - r_lo) * n; e += kBigThreads) {
+        int i = r_lo + e / n, j = e % n;
+        X[(int64_t)i * n + j] = (mode == LF_NS_INIT_REFERENCE ? P(i, j) : P(j, i)) * c0;
+    }
+    cluster.sync();
+
+    const int tpr = kBigThreads / kRB;  // 32 threads per row of the block
+    const int rr = tid / tpr, tj = tid - rr * tpr;
+    for (int it = 0; it < iters; ++it) {
+        for (int r0 = r_lo; r0 < r_hi; r0 += kRB) {
+            const int r = r0 + rr;
+            for (int j = tj; j < n; j += tpr) {
+                float acc = 0.f;
+                if (r < r_hi)
+                    for (int k = 0; k < n; ++k) acc = __fmaf_rn(X[(int64_t)r * n + k], P(k, j), acc);
+                Wr[rr * S + j] = acc;
+            }
+            __syncthreads();
+            if (r < r_hi) {
+                for (int j = tj; j < n; j += tpr) {
+                    float acc = 0.f;
+                    for (int k = 0; k < n; ++k) acc = __fmaf_rn(Wr[rr * S + k], X[(int64_t)k * n + j], acc);
+                    Vn[(r - r_lo) * S + j] = __fmaf_rn(2.f, X[(int64_t)r * n + j], -acc);
+                }
+            }
+            __syncthreads();
+        }
+        cluster.sync();  // both halves of the new iterate are complete
+        for (int e = tid; e < (r_hi - r_lo) * n; e += kBigThreads) {
+            int i = e / n, j = e % n;
+            X[(int64_t)(r_lo + i) * n + j] = Vn[i * S + j];
+        }
+        cluster.sync();  // the new iterate is visible to both CTAs
+    }
+}
+
+// dA = -(V^T G) V^T for any n, operands read from global memory (L2); used
+// where V does not fit in shared memory.
+template <typename T, typename Acc>
+__global__ void __launch_bounds__(256)
+ns_simt_bwd_global_kernel(const T* __restrict__ g, const T* __restrict__ v, T* __restrict__ da, int n) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int S = n + 1;
+    Acc* Tr = reinterpret_cast<Acc*>(smem_raw);  // [kRB][S]
+    const int tid = threadIdx.x;
+    const int64_t mat = blockIdx.x;
+    const T* G = g + mat * (int64_t)n * n;
+    const T* V = v + mat * (int64_t)n * n;
+    T* O = da + mat * (int64_t)n * n;
+    const int tpr = blockDim.x / kRB;
+    const int rr = tid / tpr, tj = tid - rr * tpr;
+    for (int r0 = 0; r0 < n; r0 += kRB) {
+        const int r = r0 + rr;
+        for (int j = tj; j < n; j += tpr) {
+            Acc acc = 0;
+            if (r < n)
+                for (int p = 0; p < n; ++p)
+                    acc = fma_acc((Acc)Elem<T>::load(V[(int64_t)p * n + r]), (Acc)Elem<T>::load(G[(int64_t)p * n + j]), acc);
+            Tr[rr * S + j] = acc;
+        }
+        __syncthreads();
+        if (r < n) {
+            for (int j = tj; j < n; j += tpr) {
+                Acc acc = 0;
+                for (int k = 0; k < n; ++k) acc = fma_acc(Tr[rr * S + k], (Acc)Elem<T>::load(V[(int64_t)j * n + k]), acc);
+                O[(int64_t)r * n + j] = Elem<T>::store(-acc);
+            }
+        }
+        __syncthreads();
+    }
+}
+
+int launch_big_fwd(const void* a, void* x, int64_t batch, int64_t n, int iters, int mode, double reg,
+                   cudaStream_t st) {
+    const size_t S = (size_t)n + 1, h = (size_t)(n + 1) / 2;
+    size_t smem = sizeof(float) * (h * S + (size_t)kRB * S + kBigThreads / 32);
+    if (smem > (size_t)max_optin_smem()) {
+        set_error("NewtonInverse: n=%lld needs %zu bytes of shared memory", (long long)n, smem);
+        return LF_ERR_UNSUPPORTED;
+    }
+    cudaFuncSetAttribute(ns_simt_big_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(2 * batch), 1, 1);
+    cfg.blockDim = dim3(kBigThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t err = cudaLaunchKernelEx(&cfg, ns_simt_big_kernel, static_cast<const float*>(a), static_cast<float*>(x),
+                                         (int)n, iters, mode, (float)reg);
+    if (err != cudaSuccess) {
+        set_error("ns_simt_big_kernel launch: %s", cudaGetErrorString(err));
+        return LF_ERR_CUDA;
+    }
+    return check_launch("ns_simt_big_kernel");
+}
+
+template <typename T>
+int launch_bwd_global(const void* g, const void* v, void* da, int64_t batch, int64_t n, cudaStream_t st) {
+    using Acc = typename Elem<T>::acc;
+    size_t smem = (size_t)kRB * ((size_t)n + 1) * sizeof(Acc);
+    auto kern = ns_simt_bwd_global_kernel<T, Acc>;
+    if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    kern<<<(unsigned)batch, 256, smem, st>>>(static_cast<const T*>(g), static_cast<const T*>(v), static_cast<T*>(da), (int)n);
+    return check_launch("ns_simt_bwd_global_kernel");
+}
+
 size_t tc_smem_bytes() { return 6 * (size_t)kOpBytes + sizeof(NsShared) + 1024; }
 
 template <typename T>
@@ -751,7 +918,7 @@ int check_ns(const void* a, const void* x, int64_t batch, int64_t n, int dtype) 
     if (dtype_size(dtype) == 0) { set_error("unsupported dtype code %d", dtype); return LF_ERR_DTYPE; }
     if (batch < 0 || n < 0) { set_error("negative size"); return LF_ERR_INVALID; }
     if (batch > 0x7fffffffLL) { set_error("batch too large"); return LF_ERR_UNSUPPORTED; }
-    if (n > kTile) { set_error("NewtonInverse supports n <= %d (got %lld)", kTile, (long long)n); return LF_ERR_UNSUPPORTED; }
+    if (n > kMaxN) { set_error("NewtonInverse supports n <= %d (got %lld)", kMaxN, (long long)n); return LF_ERR_UNSUPPORTED; }
     if (batch > 0 && n > 0 && (!a || !x)) { set_error("null pointer"); return LF_ERR_INVALID; }
     return LF_OK;
 }
@@ -761,7 +928,7 @@ int check_ns(const void* a, const void* x, int64_t batch, int64_t n, int dtype) 
 
 using namespace lfb;
 
-extern "C" int lf_newton_inverse_supported(int64_t n) { return (n >= 1 && n <= kTile) ? 1 : 0; }
+extern "C" int lf_newton_inverse_supported(int64_t n) { return (n >= 1 && n <= kMaxN) ? 1 : 0; }
 
 extern "C" int lf_newton_inverse_fwd_ex(const void* a, void* x, int64_t batch, int64_t n, int iters,
                                         int dtype, int init_mode, double reg, int precision,
@@ -780,6 +947,13 @@ extern "C" int lf_newton_inverse_fwd_ex(const void* a, void* x, int64_t batch, i
     if (batch == 0 || n == 0) return LF_OK;
     if (iters < 0) iters = 0;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (n > kTile) {
+        if (dtype != LF_F32) {
+            set_error("NewtonInverse: n=%lld > %d is supported for fp32 only", (long long)n, kTile);
+            return LF_ERR_UNSUPPORTED;
+        }
+        return launch_big_fwd(a, x, batch, n, iters, init_mode, reg, st);
+    }
     if (dtype == LF_F64) return launch_simt_fwd<double>(a, x, batch, n, iters, init_mode, reg, st);
     if (precision == LF_NS_PREC_FP32_SIMT) {
         LF_DISPATCH(dtype, T, return launch_simt_fwd<T>(a, x, batch, n, iters, init_mode, reg, st));
@@ -808,6 +982,7 @@ extern "C" int lf_newton_inverse_bwd(const void* g, const void* v, void* da, int
     if (!da && batch * n > 0) { set_error("null grad_mat"); return LF_ERR_INVALID; }
     if (batch == 0 || n == 0) return LF_OK;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (n > kTile) { LF_DISPATCH(dtype, T, return launch_bwd_global<T>(g, v, da, batch, n, st)); }
     LF_DISPATCH(dtype, T, return launch_simt_bwd<T>(g, v, da, batch, n, st));
     return LF_OK;
 }

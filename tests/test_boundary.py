@@ -42,13 +42,14 @@ def test_host_only_entry_points():
     assert L.lf_cudart_version() >= 12000
     assert L.lf_version() >= 100
     assert capi.newton_inverse_supported(1) and capi.newton_inverse_supported(128)
-    assert not capi.newton_inverse_supported(0) and not capi.newton_inverse_supported(129)
+    assert capi.newton_inverse_supported(256)
+    assert not capi.newton_inverse_supported(0) and not capi.newton_inverse_supported(257)
     # argument validation happens before any device work
     assert L.lf_laplace_sub_fwd(None, None, None, 1, 2, 3, 4, 7, None) == capi.LF_ERR_DTYPE
     assert b"dtype" in L.lf_last_error()
     assert L.lf_laplace_sub_fwd(None, None, None, 1, 2, 3, 4, 0, None) == capi.LF_ERR_INVALID
     assert L.lf_laplace_sub_fwd(None, None, None, -1, 2, 3, 4, 0, None) == capi.LF_ERR_INVALID
-    assert L.lf_newton_inverse_fwd(None, None, 1, 129, 3, 0, None) == capi.LF_ERR_UNSUPPORTED
+    assert L.lf_newton_inverse_fwd(None, None, 1, 257, 3, 0, None) == capi.LF_ERR_UNSUPPORTED
     assert L.lf_newton_inverse_fwd_ex(None, None, 1, 4, 3, 0, 7, 0.0, 0, None) == capi.LF_ERR_INVALID
     # empty problems are no-ops
     assert L.lf_laplace_sub_fwd(None, None, None, 0, 2, 3, 4, 0, None) == capi.LF_OK
@@ -65,7 +66,7 @@ def test_extension_keeps_reference_names():
     assert L.has_cuda()
     assert L.get_cuda_version().startswith("CUDA 12.")
     assert L.get_compiler_version()
-    assert L.NewtonInverse_is_supported(128) and not L.NewtonInverse_is_supported(129)
+    assert L.NewtonInverse_is_supported(256) and not L.NewtonInverse_is_supported(257)
 
 
 def test_cpu_tensors_raise_like_the_reference():

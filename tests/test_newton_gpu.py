@@ -117,12 +117,43 @@ def test_backward_vs_oracle(cuda, n, dtype):
 
 
 def test_unsupported_sizes(cuda):
-    assert capi.newton_inverse_supported(128)
-    assert not capi.newton_inverse_supported(129)
-    A = torch.randn(1, 1, 129, 129, device=cuda)
+    assert capi.newton_inverse_supported(256)
+    assert not capi.newton_inverse_supported(257)
+    A = torch.randn(1, 1, 257, 257, device=cuda)
     with pytest.raises(capi.LfError) as e:
         capi.newton_inverse_fwd(A, 3)
     assert e.value.code == capi.LF_ERR_UNSUPPORTED
+    # beyond 128 only fp32 (the iterate is kept in the output buffer)
+    with pytest.raises(capi.LfError) as e:
+        capi.newton_inverse_fwd(torch.randn(1, 1, 200, 200, device=cuda).half(), 3)
+    assert e.value.code == capi.LF_ERR_UNSUPPORTED
+
+
+@pytest.mark.parametrize("n", [129, 200, 256])
+@pytest.mark.parametrize("mode", [capi.INIT_REFERENCE, capi.INIT_SCALED_TRANSPOSE])
+def test_forward_large_n(cuda, n, mode):
+    # 128 < n <= 256 (configuration 5's landmark kernel): two-CTA cluster path.
+    A = spd(2, n, seed=n)
+    X = capi.newton_inverse_fwd(A.to(cuda), 10, init_mode=mode)
+    torch.cuda.synchronize()
+    Xr = O.newton_fwd(A.numpy(), 10, mode=mode, order=1)
+    reg = 0.01 if mode == capi.INIT_REFERENCE else 0.0
+    r_gpu = _res(A.numpy(), X.cpu().numpy(), reg)
+    r_ref = _res(A.numpy(), Xr, reg)
+    assert np.all(np.abs(r_gpu - r_ref) <= 1e-4), (r_gpu, r_ref)
+    np.testing.assert_allclose(X.cpu().numpy(), Xr, rtol=0, atol=1e-4 * np.abs(Xr).max())
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float64], ids=str)
+def test_backward_large_n(cuda, dtype):
+    g0 = torch.Generator().manual_seed(3)
+    V = torch.randn(1, 2, 256, 256, generator=g0, dtype=torch.float64).to(dtype)
+    G = torch.randn(1, 2, 256, 256, generator=g0, dtype=torch.float64).to(dtype)
+    dA = capi.newton_inverse_bwd(G.to(cuda), V.to(cuda))
+    torch.cuda.synchronize()
+    ref = O.newton_bwd(G.numpy(), V.numpy())
+    tol = 1e-5 if dtype == torch.float32 else 1e-12
+    np.testing.assert_allclose(dA.cpu().numpy(), ref, rtol=0, atol=tol * 4 * np.abs(ref).max())
 
 
 def test_extension_and_autograd(cuda, ext):
@@ -132,9 +163,9 @@ def test_extension_and_autograd(cuda, ext):
     out = torch.empty_like(A)
     ext.NewtonInverse_forward(A, out, 10)
     assert torch.equal(out, capi.newton_inverse_fwd_reference(A, 10))
-    assert ext.NewtonInverse_is_supported(128) and not ext.NewtonInverse_is_supported(129)
+    assert ext.NewtonInverse_is_supported(256) and not ext.NewtonInverse_is_supported(257)
     with pytest.raises(RuntimeError, match="not supported"):
-        big = torch.randn(1, 1, 130, 130, device=cuda)
+        big = torch.randn(1, 1, 260, 260, device=cuda)
         ext.NewtonInverse_forward(big, torch.empty_like(big), 3)
     Ad = A.double().requires_grad_()
     X = newton_inverse(Ad, 30)
