@@ -274,17 +274,13 @@ def run_b200(args, rank, world, dev):
     hs = torch.empty(s.shape, dtype=dtype).pin_memory()
     hdq = torch.empty(dq.shape, dtype=dtype).pin_memory()
     hdk = torch.empty(dk.shape, dtype=dtype).pin_memory()
-    q2, k2, g2 = torch.empty_like(q), torch.empty_like(kT), torch.empty_like(ds)
+
+    from laplacianformer_b200.streaming import HostPipeline
+
+    pipe = HostPipeline(q.shape, M, dtype=dtype, device=dev, chunks=8)
 
     def e2e_step():
-        q2.copy_(hq, non_blocking=True)
-        k2.copy_(hk, non_blocking=True)
-        g2.copy_(hg, non_blocking=True)
-        capi.laplace_sub_fwd(q2, k2, s)
-        capi.laplace_sub_bwd(g2, q2, k2, dq, dk)
-        hs.copy_(s, non_blocking=True)
-        hdq.copy_(dq, non_blocking=True)
-        hdk.copy_(dk, non_blocking=True)
+        pipe(hq, hk, hg, hs, hdq, hdk)
 
     e2e_times = time_steps(e2e_step, args.steps, args.warmup, flush, stream)
     e2e_ms = max_over_ranks(statistics.mean(e2e_times))
@@ -305,7 +301,7 @@ def run_b200(args, rank, world, dev):
         "roofline": roofline,
         "e2e": {"value": world * dists / (e2e_ms / 1e3) / 1e9, "unit": UNIT, "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "api": "laplacianformer_b200.capi (C ABI) with pinned host buffers"},
+                "api": "laplacianformer_b200.streaming.HostPipeline (C ABI, 8 B*H chunks on copy-in / kernel / copy-out streams) with pinned host buffers"},
         "gpu_launches": 2 * args.steps,
         "clocks": clk.summary(),
     }
@@ -349,6 +345,26 @@ def run_reference(args, rank, world, dev):
         times = time_steps(step, args.steps, args.warmup, flush, stream)
     ms = statistics.mean(times)
     value = B * H * N * M / (ms / 1e3) / 1e9
+    # The same end-to-end step as the B200 arm: pinned host inputs copied in,
+    # the reference operators, results copied out.
+    hq, hk, hg = q.cpu().pin_memory(), kT.cpu().pin_memory(), ds.cpu().pin_memory()
+    hs = torch.empty(s.shape, dtype=dtype).pin_memory()
+    hdq = torch.empty(dq.shape, dtype=dtype).pin_memory()
+    hdk = torch.empty(dk.shape, dtype=dtype).pin_memory()
+
+    def e2e_step():
+        q.copy_(hq, non_blocking=True)
+        kT.copy_(hk, non_blocking=True)
+        ds.copy_(hg, non_blocking=True)
+        step()
+        hs.copy_(s, non_blocking=True)
+        hdq.copy_(dq, non_blocking=True)
+        hdk.copy_(dk, non_blocking=True)
+
+    e2e_ms = statistics.mean(time_steps(e2e_step, args.steps, args.warmup, flush, stream))
+    es = q.element_size()
+    h2d = (q.numel() + kT.numel() + ds.numel()) * es
+    d2h = (s.numel() + dq.numel() + dk.numel()) * es
     # Newton–Schulz on configuration 3 with the reference operator (its own init).
     from laplacianformer_b200 import workloads as W
 
@@ -368,7 +384,9 @@ def run_reference(args, rank, world, dev):
         "device": "the reference's own CUDA operators (oracle/_ref, built from its sources for sm_100) on 1 B200",
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": 0, "kind": "reference",
                          "sample": "full workload; the reference has no CPU implementation, its CUDA kernels run on the GPU"},
-        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "e2e": {"value": B * H * N * M / (e2e_ms / 1e3) / 1e9, "unit": UNIT, "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "api": "the reference's Laplace_subtraction_cuda ops with pinned host buffers copied in and out"},
         "newton_inverse": {"value": 4096 / (nms / 1e3), "unit": "matrices/s", "ms_per_step": nms,
                            "init": "reference (A + 0.01 I, alpha = 1.8/rowsum^2)"},
         "clocks": clk.summary(),
@@ -433,6 +451,7 @@ def main():
         run_only(args, dev)
         return
     if world > 1:
+        os.environ.setdefault("NCCL_DEBUG", "WARN")  # keep stdout to the one JSON line
         torch.distributed.init_process_group("nccl", device_id=dev)
     try:
         line = run_b200(args, rank, world, dev)

@@ -594,6 +594,7 @@ lsub_bwd_fast_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* 
     A* csum = rsum + RC;                       // [MP]
     A* dkb = csum + MP;                        // [CW][KSTR]
     A* cpart = dkb + CW * geo.KSTR;            // [8][MP]
+    A* dpart = cpart + (kThreads / 32) * MP;   // [8][CW][KSTR] per-warp dKT partials
 
     cg::cluster_group cluster = cg::this_cluster();
     const int bh = blockIdx.y;
@@ -697,22 +698,25 @@ lsub_bwd_fast_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* 
         v += __shfl_xor_sync(0xffffffffu, v, 16);
         if (lane < 4) cpart[warp * MP + sq * CPT + k] = v;
     }
-    for (int e = tid; e < CW * geo.KSTR; e += kThreads) dkb[e] = A(0);
+    // Per-warp partials of -2 * sum_i g*t, combined in a fixed order so that
+    // results are bitwise reproducible.
+    if (lane_active) {
+#pragma unroll
+        for (int jj = 0; jj < MB; ++jj)
+            if (jj < m) dpart[(warp * CW + c) * geo.KSTR + jj] = A(-2) * dka[jj];
+    }
     __syncthreads();
     for (int j = tid; j < m; j += kThreads) {
         A sacc = A(0);
         for (int w = 0; w < kThreads / 32; ++w) sacc += cpart[w * MP + j];
         csum[j] = sacc;
     }
-    if (lane_active) {
-#pragma unroll
-        for (int jj = 0; jj < MB; ++jj)
-            if (jj < m) atomicAdd(&dkb[c * geo.KSTR + jj], A(-2) * dka[jj]);
-    }
     __syncthreads();
     for (int e = tid; e < d * m; e += kThreads) {
         int cc = e / m, j = e - cc * m;
-        dkb[cc * geo.KSTR + j] += csum[j];
+        A sacc = csum[j];
+        for (int w = 0; w < kThreads / 32; ++w) sacc += dpart[(w * CW + cc) * geo.KSTR + j];
+        dkb[cc * geo.KSTR + j] = sacc;
     }
     cluster.sync();
     const int cs = (int)cluster.num_blocks();
@@ -742,7 +746,8 @@ int launch_bwd_fast(const T* g, const T* q, const T* kT, T* dq, T* dk, int64_t b
     geo.DBC = 1; geo.MCN = 1; geo.RG = kThreads / 32; geo.MP = MB; geo.RC = kRowChunk;
     geo.KSTR = (int)(m | 1);
     size_t smem = sizeof(A) * ((size_t)kRowChunk * MB + (size_t)kRowChunk * 32 + kRowChunk + MB +
-                               (size_t)32 * geo.KSTR + (size_t)(kThreads / 32) * MB);
+                               (size_t)32 * geo.KSTR + (size_t)(kThreads / 32) * MB +
+                               (DK ? (size_t)(kThreads / 32) * 32 * geo.KSTR : 0));
     auto kern = lsub_bwd_fast_kernel<T, MB, DQ, DK>;
     if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     const int64_t slots = cta_slots(kern, smem);

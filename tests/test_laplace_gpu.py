@@ -266,3 +266,22 @@ def test_against_reference_module(cuda, ref_module, dtype):
     tol = _bwd_tol(dtype) if dtype != torch.float16 else 2e-2
     assert torch.all((dq.double() - dq_ref.double()).abs() <= tol * ga.sum(-1, keepdim=True) + 1e-30)
     assert torch.all((dk.double() - dk_ref.double()).abs() <= tol * ga.sum(-2).unsqueeze(-2) + 1e-30)
+
+
+def test_host_pipeline_matches_device_calls(cuda):
+    from laplacianformer_b200.streaming import HostPipeline
+
+    q, k, g = _inputs((3, 2, 130, 32, 49), torch.float32, seed=12)
+    hq, hk, hg = q.pin_memory(), k.pin_memory(), g.pin_memory()
+    hs = torch.empty(3, 2, 130, 49).pin_memory()
+    hdq = torch.empty_like(q).pin_memory()
+    hdk = torch.empty_like(k).pin_memory()
+    pipe = HostPipeline(q.shape, 49, device=cuda, chunks=4)
+    for _ in range(2):  # buffer reuse across calls
+        pipe(hq, hk, hg, hs, hdq, hdk)
+        torch.cuda.synchronize()
+        s = capi.laplace_sub_fwd(q.to(cuda), k.to(cuda))
+        dq, dk = capi.laplace_sub_bwd(g.to(cuda), q.to(cuda), k.to(cuda))
+        torch.cuda.synchronize()
+        assert torch.equal(hs, s.cpu())
+        assert torch.equal(hdq, dq.cpu()) and torch.equal(hdk, dk.cpu())
