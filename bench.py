@@ -313,9 +313,61 @@ def run_b200(args, rank, world, dev):
     return line
 
 
+def run_config5(args, rank, world, dev):
+    """Configuration 5: B=8, H=16, D=64, M=256 chunk-mean landmarks, bf16 Q/K,
+    LaplaceSub fwd+bwd plus the 256x256 landmark-kernel inverse (fp32, 10
+    iterations).  Strong scaling: the 128 (b,h) slices are split over ranks."""
+    from laplacianformer_b200 import capi, workloads
+    from laplacianformer_b200.sharding import shard_bounds
+
+    stream = torch.cuda.current_stream(dev)
+    flush = _flush_buffer(dev)
+    B, H, D, M, N = 8, 16, 64, 256, args.n_tokens
+    lo, hi = shard_bounds(B * H, world, rank)
+    bh = hi - lo
+    g = torch.Generator(device=dev)
+    g.manual_seed(1000 + rank)
+    q = torch.randn(1, bh, N, D, generator=g, device=dev).to(torch.bfloat16)
+    k = torch.randn(1, bh, N, D, generator=g, device=dev).to(torch.bfloat16)
+    L = workloads.chunk_mean_landmarks(k, M)
+    kT = L.transpose(-1, -2).contiguous()
+    ds = torch.randn(1, bh, N, M, generator=g, device=dev).to(torch.bfloat16)
+    s = torch.empty(1, bh, N, M, device=dev, dtype=torch.bfloat16)
+    dq, dk = torch.empty_like(q), torch.empty_like(kT)
+    Lf = L.float().contiguous()
+    LfT = Lf.transpose(-1, -2).contiguous()
+    sll = torch.empty(1, bh, M, M, device=dev)
+    X = torch.empty_like(sll)
+    sigma = math.sqrt(D)
+
+    def step():
+        capi.laplace_sub_fwd(q, kT, s)
+        capi.laplace_sub_bwd(ds, q, kT, dq, dk)
+        capi.laplace_sub_fwd(Lf, LfT, sll)
+        A = torch.exp(sll * (-1.0 / sigma))
+        capi.newton_inverse_fwd(A, 10, out=X)
+
+    times = time_steps(step, args.steps, args.warmup, flush, stream)
+    ms = max_over_ranks(statistics.mean(times))
+    return {
+        "metric": METRIC, "value": B * H * N * M / (ms / 1e3) / 1e9, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1), configuration-5 shapes)",
+        "config": {"workload": f"config5 N={N}: LaplaceSub fwd+bwd bf16 (M=256, D=64) + NewtonInverse 256x256 fp32 x10",
+                   "global_batch": B, "heads": H, "seq_len": N, "parallelism": f"bh-shard x{world} (strong), no collective",
+                   "l2": "inputs larger than L2" if N >= 16384 else "flushed between timed steps"},
+        "newton_matrices_per_s": B * H / (ms / 1e3),
+    }
+
+
 def run_reference(args, rank, world, dev):
     from oracle.build_ref import load_ref
 
+    if args.workload == "config5":
+        return {"impl": "reference", "unavailable": "configuration 5 needs bf16 LaplaceSubtraction (no bf16 dispatch, "
+                "LaplaceSubtraction_cuda_kernel.cu:471), n = 256 NewtonInverse (rejected above 128, "
+                "NewtonInverse_cuda_kernel.cu:726) and 64-bit offsets (int indexing overflows at N = 262144)"}
     ref = load_ref()
     if ref is None:
         return {"impl": "reference", "unavailable": "oracle/_ref/Laplace_subtraction_cuda_ref.so not built "
@@ -430,6 +482,8 @@ def main():
     ap.add_argument("--only", choices=["laplace", "newton"], default=None,
                     help="profiling aid: run one workload only and print its timings")
     ap.add_argument("--ns-batch", type=int, default=4096)
+    ap.add_argument("--workload", choices=["config2", "config5"], default="config2")
+    ap.add_argument("--n-tokens", type=int, default=16384, help="configuration-5 sequence length")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
@@ -454,7 +508,7 @@ def main():
         os.environ.setdefault("NCCL_DEBUG", "WARN")  # keep stdout to the one JSON line
         torch.distributed.init_process_group("nccl", device_id=dev)
     try:
-        line = run_b200(args, rank, world, dev)
+        line = run_config5(args, rank, world, dev) if args.workload == "config5" else run_b200(args, rank, world, dev)
         if rank == 0:
             print(json.dumps(line), flush=True)
     finally:
