@@ -304,6 +304,8 @@ int launch_fwd(const void* q, const void* kT, void* s, int64_t bh, int64_t n, in
                     default: return launch_fwd_mc<T, 4, 8, 16>(Q, K, S, bh, n, m, d, st);
                 }
             }
+            if (variant == 5) return launch_fwd_mc<T, 1, 4, 32>(Q, K, S, bh, n, m, d, st);
+            if (variant == 6) return launch_fwd_mc<T, 1, 5, 32>(Q, K, S, bh, n, m, d, st);
             if (variant == 2) {
                 switch (pick_mc(m)) {
                     case 4: return launch_fwd_mc<T, 2, 4, 16>(Q, K, S, bh, n, m, d, st);
