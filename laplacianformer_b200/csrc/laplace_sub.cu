@@ -784,6 +784,244 @@ int launch_bwd_fast(const T* g, const T* q, const T* kT, T* dq, T* dk, int64_t b
     return check_launch("lsub_bwd_fast_kernel");
 }
 
+// Wide variant of the fused backward: d <= 64 and m <= 256 (configuration 5:
+// d = 64, m = 256).  Landmarks are padded to MPT = 64 * MCNT; warp w handles
+// channel block w % DBT, landmark chunk (w / DBT) % MCNT (64 landmarks) and
+// row group w / (DBT * MCNT).  Staging: thread t owns landmark column
+// t % MPT of every staged row it loads, so column sums of dS stay in one
+// register; row sums go through warp shuffles and a small shared array.  The
+// next chunk is prefetched into registers during compute.  dQ partials of the
+// landmark chunks and dK partials of the row groups are combined in a fixed
+// order (bitwise reproducible); the row-split CTAs of one (b,h) form a
+// cluster and add their dK through distributed shared memory.
+template <typename T, int DBT, int MCNT>
+__global__ void __launch_bounds__(kThreads, 1)
+lsub_bwd_wide_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* __restrict__ kT,
+                     T* __restrict__ dq, T* __restrict__ dk, BwdGeom geo) {
+    using A = typename Elem<T>::acc;
+    constexpr int MB = 64;
+    constexpr int MPT = MB * MCNT;             // padded landmarks
+    constexpr int CW = 32 * DBT;               // channels per CTA
+    constexpr int RG = (kThreads / 32) / (DBT * MCNT);
+    constexpr int RC = 4096 / MPT;             // staged rows per chunk (16 values per thread)
+    constexpr int GPT = RC * MPT / kThreads;   // dS values staged per thread (= 16)
+    constexpr int QPT = RC * CW / kThreads;    // Q values staged per thread
+    constexpr int WPR = MPT / 32;              // warps spanning one staged row
+    static_assert(RG >= 1 && GPT == 16 && QPT >= 1, "bad wide backward shape");
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int n = geo.n, m = geo.m, d = geo.d, KSTR = geo.KSTR;
+    A* gs = reinterpret_cast<A*>(smem_raw);        // [RC][MPT]
+    A* qs = gs + RC * MPT;                          // [RC][CW]
+    A* rpart = qs + RC * CW;                        // [RC][WPR]
+    A* csum = rpart + RC * WPR;                     // [MPT]
+    A* cpart = csum + MPT;                          // [kThreads / MPT][MPT]
+    A* dqp = cpart + (kThreads / MPT) * MPT;        // [MCNT][RC][CW]
+    A* dkb = dqp + MCNT * RC * CW;                  // [CW][KSTR]
+    A* dpart = dkb + CW * KSTR;                     // [RG][CW][KSTR] (RG > 1)
+
+    cg::cluster_group cluster = cg::this_cluster();
+    const int bh = blockIdx.y;
+    const int split = blockIdx.x;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int db = warp % DBT, mcb = (warp / DBT) % MCNT, rg = warp / (DBT * MCNT);
+    const int cl = db * 32 + lane, c = cl;
+    const bool lane_active = c < d;
+    const int j0 = mcb * MB;
+    const int sj = tid % MPT, srow0 = tid / MPT;    // staging column / first row
+    constexpr int SRS = kThreads / MPT;             // staging row stride
+
+    const T* Gb = g + (int64_t)bh * n * m;
+    const T* Qb = q + (int64_t)bh * n * d;
+    const T* Kb = kT + (int64_t)bh * d * m;
+
+    A kreg[MB], dka[MB];
+#pragma unroll
+    for (int jj = 0; jj < MB; ++jj) {
+        const int j = j0 + jj;
+        kreg[jj] = (lane_active && j < m) ? Elem<T>::load(Kb[(int64_t)c * m + j]) : A(0);
+        dka[jj] = A(0);
+    }
+    A colacc = A(0);
+
+    const int64_t r_begin = (int64_t)split * geo.rows_per_cta;
+    const int64_t r_end = (r_begin + geo.rows_per_cta < (int64_t)n) ? r_begin + geo.rows_per_cta : (int64_t)n;
+
+    A pg[GPT], pq[QPT];
+    auto load_chunk = [&](int64_t rc) {
+#pragma unroll
+        for (int k = 0; k < GPT; ++k) {
+            const int64_t row = rc + srow0 + SRS * k;
+            pg[k] = (row < r_end && sj < m) ? Elem<T>::load(Gb[row * m + sj]) : A(0);
+        }
+#pragma unroll
+        for (int k = 0; k < QPT; ++k) {
+            const int e = tid + kThreads * k;
+            const int i = e / CW, x = e % CW;
+            const int64_t row = rc + i;
+            pq[k] = (row < r_end && x < d) ? Elem<T>::load(Qb[row * d + x]) : A(0);
+        }
+    };
+    if (r_begin < r_end) load_chunk(r_begin);
+
+    for (int64_t rc = r_begin; rc < r_end; rc += RC) {
+        const int rows = (int)((r_end - rc) < RC ? (r_end - rc) : RC);
+        __syncthreads();  // previous chunk fully consumed
+#pragma unroll
+        for (int k = 0; k < GPT; ++k) {
+            const int i = srow0 + SRS * k;
+            gs[i * MPT + sj] = pg[k];
+            colacc += pg[k];
+            A rs = pg[k];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) rs += __shfl_xor_sync(0xffffffffu, rs, o);
+            if (lane == 0) rpart[i * WPR + (sj >> 5)] = rs;
+        }
+#pragma unroll
+        for (int k = 0; k < QPT; ++k) qs[tid + kThreads * k] = pq[k];
+        __syncthreads();
+        if (rc + RC < r_end) load_chunk(rc + RC);
+
+        if (lane_active) {
+#pragma unroll 1
+            for (int i = rg; i < rows; i += RG) {
+                const A qv = qs[i * CW + cl];
+                const A* grow = gs + i * MPT + j0;
+                A dqa = A(0);
+#pragma unroll
+                for (int j4 = 0; j4 < MB; j4 += 4) {
+                    A gv[4];
+                    if constexpr (sizeof(A) == 4) {
+                        float4 t4 = *reinterpret_cast<const float4*>(grow + j4);
+                        gv[0] = t4.x; gv[1] = t4.y; gv[2] = t4.z; gv[3] = t4.w;
+                        bwd_quad<true, true>(qv, kreg[j4], kreg[j4 + 1], kreg[j4 + 2], kreg[j4 + 3], gv, dqa,
+                                             dka[j4], dka[j4 + 1], dka[j4 + 2], dka[j4 + 3]);
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            gv[e] = grow[j4 + e];
+                            const A t = step_of<A>(qv, kreg[j4 + e]);
+                            dqa = fma_acc(gv[e], t, dqa);
+                            dka[j4 + e] = fma_acc(gv[e], t, dka[j4 + e]);
+                        }
+                    }
+                }
+                dqp[(mcb * RC + i) * CW + cl] = dqa;
+            }
+        }
+        __syncthreads();
+        // dQ = 2 * sum over landmark chunks (fixed order) - row sum of dS
+        for (int e = tid; e < rows * CW; e += kThreads) {
+            const int i = e / CW, x = e % CW;
+            if (x >= d) continue;
+            A acc = A(0);
+#pragma unroll
+            for (int b = 0; b < MCNT; ++b) acc += dqp[(b * RC + i) * CW + x];
+            A rs = A(0);
+#pragma unroll
+            for (int w = 0; w < WPR; ++w) rs += rpart[i * WPR + w];
+            dq[((int64_t)bh * n + rc + i) * d + x] = Elem<T>::store(A(2) * acc - rs);
+        }
+    }
+
+    // Column sums of dS over the CTA's rows, then dKT = csum - 2 sum g*t.
+    cpart[srow0 * MPT + sj] = colacc;
+    if (lane_active) {
+#pragma unroll
+        for (int jj = 0; jj < MB; ++jj) {
+            const int j = j0 + jj;
+            if (j < m) {
+                if (RG == 1) dkb[cl * KSTR + j] = A(-2) * dka[jj];
+                else dpart[(rg * CW + cl) * KSTR + j] = A(-2) * dka[jj];
+            }
+        }
+    }
+    __syncthreads();
+    for (int j = tid; j < m; j += kThreads) {
+        A s = A(0);
+        for (int r = 0; r < SRS; ++r) s += cpart[r * MPT + j];
+        csum[j] = s;
+    }
+    __syncthreads();
+    for (int e = tid; e < CW * m; e += kThreads) {
+        const int cc = e / m, j = e % m;
+        if (cc >= d) continue;
+        A s = csum[j];
+        if (RG == 1) {
+            s += dkb[cc * KSTR + j];
+        } else {
+            for (int r = 0; r < RG; ++r) s += dpart[(r * CW + cc) * KSTR + j];
+        }
+        dkb[cc * KSTR + j] = s;
+    }
+    cluster.sync();
+    const int cs = (int)cluster.num_blocks();
+    const int rank = (int)cluster.block_rank();
+    const int total = d * m;
+    const int per = (total + cs - 1) / cs;
+    const int e0 = rank * per, e1 = min(total, e0 + per);
+    T* dkout = dk + (int64_t)bh * d * m;
+    for (int e = e0 + tid; e < e1; e += kThreads) {
+        const int cc = e / m, j = e - cc * m;
+        A s = A(0);
+        for (int r = 0; r < cs; ++r) {
+            const A* peer = cluster.map_shared_rank(dkb, r);
+            s += peer[cc * KSTR + j];
+        }
+        dkout[e] = Elem<T>::store(s);
+    }
+    cluster.sync();
+}
+
+template <typename T, int DBT, int MCNT>
+int launch_bwd_wide(const T* g, const T* q, const T* kT, T* dq, T* dk, int64_t bh, int64_t n, int64_t m,
+                    int64_t d, cudaStream_t st) {
+    using A = typename Elem<T>::acc;
+    constexpr int MPT = 64 * MCNT, CW = 32 * DBT, RG = 8 / (DBT * MCNT), RC = 4096 / MPT;
+    BwdGeom geo;
+    geo.n = (int)n; geo.m = (int)m; geo.d = (int)d;
+    geo.DBC = DBT; geo.MCN = MCNT; geo.RG = RG; geo.MP = MPT; geo.RC = RC;
+    geo.KSTR = (int)(m | 1);
+    size_t smem = sizeof(A) * ((size_t)RC * MPT + (size_t)RC * CW + (size_t)RC * (MPT / 32) + MPT +
+                               (size_t)(kThreads / MPT) * MPT + (size_t)MCNT * RC * CW + (size_t)CW * geo.KSTR +
+                               (RG > 1 ? (size_t)RG * CW * geo.KSTR : 0));
+    if (smem > (size_t)max_optin_smem()) {
+        set_error("LaplaceSubtraction backward: needs %zu bytes of shared memory", smem);
+        return LF_ERR_UNSUPPORTED;
+    }
+    auto kern = lsub_bwd_wide_kernel<T, DBT, MCNT>;
+    if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    const int64_t slots = cta_slots(kern, smem);
+    const int64_t max_by_rows = (n + RC - 1) / RC;
+    int64_t cs = 1;
+    double best = -1.0;
+    for (int64_t c = 1; c <= 8 && c <= (max_by_rows < 1 ? 1 : max_by_rows); ++c) {
+        double eff = wave_efficiency(bh * c, slots);
+        if (eff > best + 1e-9) { best = eff; cs = c; }
+    }
+    int64_t rpc = (n + cs - 1) / cs;
+    rpc = ((rpc + RC - 1) / RC) * RC;
+    geo.rows_per_cta = (int)rpc;
+    if (bh > 65535) { set_error("b*h = %lld exceeds 65535", (long long)bh); return LF_ERR_UNSUPPORTED; }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)cs, (unsigned)bh, 1);
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)cs;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t err = cudaLaunchKernelEx(&cfg, kern, g, q, kT, dq, dk, geo);
+    if (err != cudaSuccess) {
+        set_error("lsub_bwd_wide_kernel launch: %s", cudaGetErrorString(err));
+        return LF_ERR_CUDA;
+    }
+    return check_launch("lsub_bwd_wide_kernel");
+}
+
 // Landmark chunk per warp (MB) and number of chunks (mcn): least padding of m
 // with at most 8 chunks; ties prefer chunks of at most 52 landmarks (larger
 // ones spill registers in the fused kernel), then the larger chunk.
@@ -894,6 +1132,19 @@ int launch_bwd_t(const void* g, const void* q, const void* kT, void* dq, void* d
                 case 56: return launch_bwd_fast<T, 56, DQ, DK>(G, Q, K, DQp, DKp, bh, n, m, d, st);
                 default: return launch_bwd_fast<T, 64, DQ, DK>(G, Q, K, DQp, DKp, bh, n, m, d, st);
             }
+        }
+    }
+    if constexpr (sizeof(T) != 8) {
+        // wide path (both gradients): d <= 64, 64 < m <= 256 or 32 < d <= 64
+        if (DQ && DK && d <= 64 && m <= 256 && (m > 64 || d > 32)) {
+            const int mc = m <= 64 ? 1 : (m <= 128 ? 2 : 4);
+            if (d <= 32) {
+                if (mc == 2) return launch_bwd_wide<T, 1, 2>(G, Q, K, DQp, DKp, bh, n, m, d, st);
+                return launch_bwd_wide<T, 1, 4>(G, Q, K, DQp, DKp, bh, n, m, d, st);
+            }
+            if (mc == 1) return launch_bwd_wide<T, 2, 1>(G, Q, K, DQp, DKp, bh, n, m, d, st);
+            if (mc == 2) return launch_bwd_wide<T, 2, 2>(G, Q, K, DQp, DKp, bh, n, m, d, st);
+            return launch_bwd_wide<T, 2, 4>(G, Q, K, DQp, DKp, bh, n, m, d, st);
         }
     }
     int mcn = 1;

@@ -62,6 +62,7 @@ namespace {
 constexpr int kNsThreads = 512;
 constexpr int kTile = 128;                 // padded matrix size
 constexpr int kOpBytes = kTile * kTile * 2; // one fp16 operand (32 KB)
+constexpr bool kWInTmem = true;        // W operand of the second product in TMEM (else shared memory)
 constexpr bool kSplitW = false;        // W = V P as two N = 64 halves (true) or one N = 128 product
 constexpr int kTmemCols = 512;             // W and Y accumulators + fp32 V (384 used)
 
@@ -123,6 +124,16 @@ __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_
         "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
+// D[tmem] (+)= A[tmem] * B[smem], kind::f16: A is 128 lanes (rows) x K fp16
+// with consecutive K pairs packed in one 32-bit column.
+__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
@@ -151,6 +162,14 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) 
         "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),
         "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]),
         "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
         : "memory");
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
@@ -226,6 +245,32 @@ __device__ __forceinline__ void named_sync(int id, int count) {
 }
 __device__ __forceinline__ void named_arrive(int id, int count) {
     asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+// hi/lo fp16 split of 32 values into packed pairs (element 2i in the low half).
+__device__ __forceinline__ void split_pack(const float (&v)[32], float s, uint32_t (&h)[16], uint32_t (&l)[16]) {
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+        const float2 xs = make_float2(v[2 * e] * s, v[2 * e + 1] * s);
+        const __half2 hh = __float22half2_rn(xs);
+        const float2 hb = __half22float2(hh);
+        const __half2 ll = __float22half2_rn(make_float2(xs.x - hb.x, xs.y - hb.y));
+        h[e] = *reinterpret_cast<const uint32_t*>(&hh);
+        l[e] = *reinterpret_cast<const uint32_t*>(&ll);
+    }
+}
+
+// Y += W * V for K steps [ks0, ks1) with W (hi at a_hi, lo at a_lo) in TMEM.
+__device__ __forceinline__ void issue_mma_ts(uint32_t acc, uint32_t a_hi, uint32_t a_lo, uint32_t b_hi,
+                                             uint32_t b_lo, int ks0, int ks1, int nterm, bool first) {
+    constexpr uint32_t idesc = (1u << 4) | (1u << 16) | ((uint32_t)(kTile >> 3) << 17) | ((uint32_t)(kTile >> 4) << 24);
+    for (int ks = ks0; ks < ks1; ++ks) {
+        mma_f16_ts(acc, a_hi + ks * 8, desc_b(b_hi, ks), idesc, (first && ks == ks0) ? 0u : 1u);
+        if (nterm == 3) {
+            mma_f16_ts(acc, a_hi + ks * 8, desc_b(b_lo, ks), idesc, 1u);
+            mma_f16_ts(acc, a_lo + ks * 8, desc_b(b_hi, ks), idesc, 1u);
+        }
+    }
 }
 
 struct NsShared {
@@ -367,6 +412,8 @@ ns_tc_fwd_kernel(const T* __restrict__ a, T* __restrict__ x, int n, int iters, i
     const uint32_t t_w = tmem + t_lane;              // W accumulator, columns [0,128)
     const uint32_t t_y = tmem + t_lane + kTile;      // Y accumulator, columns [128,256)
     const uint32_t t_v = tmem + t_lane + 2 * kTile;  // fp32 V, columns [256,384)
+    const uint32_t t_wa = tmem + t_lane + 3 * kTile;  // W hi [384,448) and lo [448,512), fp16 pairs
+    const uint32_t a_whi = tmem + 3 * kTile, a_wlo = tmem + 3 * kTile + kTile / 2;  // as MMA A operands
     {
         float pv[32], vv[32];
 #pragma unroll
@@ -429,7 +476,15 @@ ns_tc_fwd_kernel(const T* __restrict__ a, T* __restrict__ x, int n, int iters, i
             reg_fence(wv);
             NS_TRACE(it, 12);
             // acc = W * sV * sP; the stored operand is W * sW (all powers of two)
-            split_store(Wh, Wl, row, col0, wv, sW * (1.f / sV) * (1.f / sP));
+            if (kWInTmem) {
+                uint32_t hp[16], lp[16];
+                split_pack(wv, sW * (1.f / sV) * (1.f / sP), hp, lp);
+                tmem_st16(t_wa + col0 / 2, hp);
+                tmem_st16(t_wa + kTile / 2 + col0 / 2, lp);
+                tmem_wait_st();
+            } else {
+                split_store(Wh, Wl, row, col0, wv, sW * (1.f / sV) * (1.f / sP));
+            }
         }
         NS_TRACE(it, 3);
         fence_async_smem();
@@ -439,13 +494,15 @@ ns_tc_fwd_kernel(const T* __restrict__ a, T* __restrict__ x, int n, int iters, i
             named_sync(1, kNsThreads / 2);
             if (tid == 0) {
                 tc_fence_after();
-                issue_mma<128>(tmem + kTile, aWh, aWl, aVh, aVl, 0, kTile / 32, nterm, true);
+                if (kWInTmem) issue_mma_ts(tmem + kTile, a_whi, a_wlo, aVh, aVl, 0, kTile / 32, nterm, true);
+                else issue_mma<128>(tmem + kTile, aWh, aWl, aVh, aVl, 0, kTile / 32, nterm, true);
             }
             if (warp == 0) {
                 named_sync(2, kNsThreads / 2 + 32);
                 if (lane == 0) {
                     tc_fence_after();
-                    issue_mma<128>(tmem + kTile, aWh, aWl, aVh, aVl, kTile / 32, kTile / 16, nterm, false);
+                    if (kWInTmem) issue_mma_ts(tmem + kTile, a_whi, a_wlo, aVh, aVl, kTile / 32, kTile / 16, nterm, false);
+                    else issue_mma<128>(tmem + kTile, aWh, aWl, aVh, aVl, kTile / 32, kTile / 16, nterm, false);
                     mma_commit(&sh.bar[2]);
                 }
                 __syncwarp();
