@@ -168,6 +168,13 @@ LF_API int lf_newton_inverse_residual(const void* a, const void* x, void* res,
    errors (src/NewtonInverse_cuda_kernel.cu:790-793). */
 LF_API int lf_device_status(int clear);
 
+/* Launches a one-block kernel that waits on a barrier nothing completes; the
+   bounded wait gives up after timeout_ms (1..10000) and records LF_ERR_TIMEOUT
+   in the device status word (read it with lf_device_status).  Exercises the
+   error path the tensor-core kernels take instead of hanging.  No
+   counterpart in the reference. */
+LF_API int lf_selftest_bounded_wait(int timeout_ms, lf_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -43,6 +43,7 @@ SIGNATURES = {
     "lf_newton_inverse_bwd": (_I, [_P, _P, _P, _I64, _I64, _I, _P]),
     "lf_newton_inverse_residual": (_I, [_P, _P, _P, _I64, _I64, _D, _I, _P]),
     "lf_device_status": (_I, [_I]),
+    "lf_selftest_bounded_wait": (_I, [_I, _P]),
 }
 
 _lib = None

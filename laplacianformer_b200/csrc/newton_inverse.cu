@@ -86,7 +86,7 @@ __device__ __forceinline__ uint64_t global_ns() {
 // Returns true when the phase with the given parity has completed, false if
 // it has not completed within about two seconds (bounded wait; the caller
 // reports LF_ERR_TIMEOUT instead of hanging the GPU).
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns = 2000000000ull) {
     const uint32_t addr = smem_u32(bar);
     const uint64_t t0 = global_ns();
     for (uint32_t spin = 0;; ++spin) {
@@ -99,7 +99,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
             : "r"(addr), "r"(parity)
             : "memory");
         if (done) return true;
-        if ((spin & 255u) == 255u && global_ns() - t0 > 2000000000ull) return false;
+        if ((spin & 255u) == 255u && global_ns() - t0 > limit_ns) return false;
     }
 }
 
@@ -759,17 +759,69 @@ constexpr int kBigThreads = 512;
 // [r*h, min(n, (r+1)*h)), h = ceil(n/2).  The current iterate V lives in the
 // output buffer (global memory, L2-resident) and the CTA's rows of the next
 // iterate in shared memory; once both halves are complete (cluster barrier)
-// they are written back.  W = V P and Y = W V are formed 16 rows at a time:
-// the reference 2-buffer association (V P) V.
+// they are written back.  Per block of 32 rows, W = V P and Y = W V are tiled
+// FMA products (32-wide K chunks staged in shared memory, 4x4 outputs per
+// thread): the reference 2-buffer association (V P) V.
+constexpr int kBigRB = 32;   // rows per block
+constexpr int kBigKC = 32;   // K chunk
+constexpr int kBigCols = 256;
+
+struct BigTile {
+    float* As;  // [kBigRB][kBigKC + 1]
+    float* Bs;  // [kBigKC][kBigCols]
+};
+
+// acc[4][4] += Arows[32 x n] * B[n x 256] for this thread's 4x4 tile, with
+// A(i, k) and B(k, j) supplied by functors (zero outside the matrix).
+template <typename FA, typename FB>
+__device__ __forceinline__ void big_tile_gemm(float (&acc)[4][4], int n, const BigTile& t, FA a_at, FB b_row4) {
+    const int tid = threadIdx.x;
+    const int tr = tid >> 6, tc = tid & 63;  // 8 row groups x 64 column groups
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+    for (int k0 = 0; k0 < n; k0 += kBigKC) {
+        __syncthreads();
+        for (int e = tid; e < kBigRB * kBigKC; e += kBigThreads) {
+            const int i = e / kBigKC, kk = e % kBigKC;
+            t.As[i * (kBigKC + 1) + kk] = (k0 + kk < n) ? a_at(i, k0 + kk) : 0.f;
+        }
+        for (int e = tid; e < kBigKC * (kBigCols / 4); e += kBigThreads) {
+            const int kk = e / (kBigCols / 4), j4 = e % (kBigCols / 4);
+            float4 v = (k0 + kk < n) ? b_row4(k0 + kk, 4 * j4) : make_float4(0.f, 0.f, 0.f, 0.f);
+            *reinterpret_cast<float4*>(&t.Bs[kk * kBigCols + 4 * j4]) = v;
+        }
+        __syncthreads();
+#pragma unroll 8
+        for (int kk = 0; kk < kBigKC; ++kk) {
+            const float4 b = *reinterpret_cast<const float4*>(&t.Bs[kk * kBigCols + 4 * tc]);
+            float a[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) a[i] = t.As[(4 * tr + i) * (kBigKC + 1) + kk];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                acc[i][0] = __fmaf_rn(a[i], b.x, acc[i][0]);
+                acc[i][1] = __fmaf_rn(a[i], b.y, acc[i][1]);
+                acc[i][2] = __fmaf_rn(a[i], b.z, acc[i][2]);
+                acc[i][3] = __fmaf_rn(a[i], b.w, acc[i][3]);
+            }
+        }
+    }
+}
+
 __global__ void __launch_bounds__(kBigThreads, 1)
 ns_simt_big_kernel(const float* __restrict__ a, float* __restrict__ x, int n, int iters, int mode, float reg) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     cg::cluster_group cluster = cg::this_cluster();
-    const int S = n + 1;
     const int h = (n + 1) / 2;
-    float* Vn = reinterpret_cast<float*>(smem_raw);  // [h][S]
-    float* Wr = Vn + (size_t)h * S;                   // [kRB][S]
-    float* red = Wr + kRB * S;                        // [kBigThreads/32]
+    float* Vn = reinterpret_cast<float*>(smem_raw);        // [h][kBigCols]
+    float* Wb = Vn + (size_t)h * kBigCols;                  // [kBigRB][kBigCols]
+    BigTile t;
+    t.As = Wb + kBigRB * kBigCols;                          // [kBigRB][kBigKC+1]
+    t.Bs = t.As + kBigRB * (kBigKC + 1) + 3;                // [kBigKC][kBigCols] (16-byte aligned)
+    t.Bs = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(t.Bs) + 15) & ~uintptr_t(15));
+    float* red = t.Bs + kBigKC * kBigCols;                  // [kBigThreads/32]
     const int tid = threadIdx.x;
     const int rank = (int)cluster.block_rank();
     const int64_t mat = blockIdx.x / 2;
@@ -777,6 +829,20 @@ ns_simt_big_kernel(const float* __restrict__ a, float* __restrict__ x, int n, in
     float* X = x + mat * (int64_t)n * n;
     const int r_lo = rank * h, r_hi = min(n, r_lo + h);
     auto P = [&](int i, int j) -> float { return A[(int64_t)i * n + j] + (i == j ? reg : 0.f); };
+    const bool vec = (n % 4) == 0;
+    auto row4 = [&](const float* base, int k, int j, bool add_reg) -> float4 {
+        float4 v;
+        if (vec && j + 3 < n) {
+            v = *reinterpret_cast<const float4*>(base + (int64_t)k * n + j);
+        } else {
+            v.x = j < n ? base[(int64_t)k * n + j] : 0.f;
+            v.y = j + 1 < n ? base[(int64_t)k * n + j + 1] : 0.f;
+            v.z = j + 2 < n ? base[(int64_t)k * n + j + 2] : 0.f;
+            v.w = j + 3 < n ? base[(int64_t)k * n + j + 3] : 0.f;
+        }
+        if (add_reg && k >= j && k < j + 4) (&v.x)[k - j] += reg;
+        return v;
+    };
 
     float c0;
     if (mode == LF_NS_INIT_REFERENCE) {
@@ -806,31 +872,38 @@ ns_simt_big_kernel(const float* __restrict__ a, float* __restrict__ x, int n, in
     }
     cluster.sync();
 
-    const int tpr = kBigThreads / kRB;  // 32 threads per row of the block
-    const int rr = tid / tpr, tj = tid - rr * tpr;
+    const int tr = tid >> 6, tc = tid & 63;
     for (int it = 0; it < iters; ++it) {
-        for (int r0 = r_lo; r0 < r_hi; r0 += kRB) {
-            const int r = r0 + rr;
-            for (int j = tj; j < n; j += tpr) {
-                float acc = 0.f;
-                if (r < r_hi)
-                    for (int k = 0; k < n; ++k) acc = __fmaf_rn(X[(int64_t)r * n + k], P(k, j), acc);
-                Wr[rr * S + j] = acc;
-            }
-            __syncthreads();
-            if (r < r_hi) {
-                for (int j = tj; j < n; j += tpr) {
-                    float acc = 0.f;
-                    for (int k = 0; k < n; ++k) acc = __fmaf_rn(Wr[rr * S + k], X[(int64_t)k * n + j], acc);
-                    Vn[(r - r_lo) * S + j] = __fmaf_rn(2.f, X[(int64_t)r * n + j], -acc);
+        for (int r0 = r_lo; r0 < r_hi; r0 += kBigRB) {
+            const int rows = min(kBigRB, r_hi - r0);
+            float acc[4][4];
+            // W[r0 .. r0+31, :] = V[r0 .., :] P
+            big_tile_gemm(acc, n, t,
+                          [&](int i, int k) { return i < rows ? X[(int64_t)(r0 + i) * n + k] : 0.f; },
+                          [&](int k, int j) { return row4(A, k, j, true); });
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                *reinterpret_cast<float4*>(&Wb[(4 * tr + i) * kBigCols + 4 * tc]) =
+                    make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+            // Y = W V;  V'[r] = 2 V[r] - Y[r]
+            big_tile_gemm(acc, n, t, [&](int i, int k) { return Wb[i * kBigCols + k]; },
+                          [&](int k, int j) { return row4(X, k, j, false); });
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int r = 4 * tr + i;
+                if (r >= rows) continue;
+#pragma unroll
+                for (int jj = 0; jj < 4; ++jj) {
+                    const int j = 4 * tc + jj;
+                    if (j < n)
+                        Vn[(r0 - r_lo + r) * kBigCols + j] = __fmaf_rn(2.f, X[(int64_t)(r0 + r) * n + j], -acc[i][jj]);
                 }
             }
-            __syncthreads();
         }
         cluster.sync();  // both halves of the new iterate are complete
         for (int e = tid; e < (r_hi - r_lo) * n; e += kBigThreads) {
             int i = e / n, j = e % n;
-            X[(int64_t)(r_lo + i) * n + j] = Vn[i * S + j];
+            X[(int64_t)(r_lo + i) * n + j] = Vn[i * kBigCols + j];
         }
         cluster.sync();  // the new iterate is visible to both CTAs
     }
@@ -874,8 +947,9 @@ ns_simt_bwd_global_kernel(const T* __restrict__ g, const T* __restrict__ v, T* _
 
 int launch_big_fwd(const void* a, void* x, int64_t batch, int64_t n, int iters, int mode, double reg,
                    cudaStream_t st) {
-    const size_t S = (size_t)n + 1, h = (size_t)(n + 1) / 2;
-    size_t smem = sizeof(float) * (h * S + (size_t)kRB * S + kBigThreads / 32);
+    const size_t h = (size_t)(n + 1) / 2;
+    size_t smem = sizeof(float) * (h * kBigCols + (size_t)kBigRB * kBigCols + (size_t)kBigRB * (kBigKC + 1) + 8 +
+                                   (size_t)kBigKC * kBigCols + kBigThreads / 32);
     if (smem > (size_t)max_optin_smem()) {
         set_error("NewtonInverse: n=%lld needs %zu bytes of shared memory", (long long)n, smem);
         return LF_ERR_UNSUPPORTED;
@@ -910,6 +984,18 @@ int launch_bwd_global(const void* g, const void* v, void* da, int64_t batch, int
     if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     kern<<<(unsigned)batch, 256, smem, st>>>(static_cast<const T*>(g), static_cast<const T*>(v), static_cast<T*>(da), (int)n);
     return check_launch("ns_simt_bwd_global_kernel");
+}
+
+// Self-test of the bounded-wait error path: one CTA waits on an mbarrier that
+// nothing arrives at; the wait gives up after `limit_ns` and the kernel
+// records LF_ERR_TIMEOUT in the device status word, as the tensor-core kernel
+// does, and returns normally.
+__global__ void bounded_wait_probe_kernel(uint64_t limit_ns) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) mbar_init(&bar, 1);
+    __syncthreads();
+    const bool ok = mbar_wait(&bar, 0, limit_ns);
+    if (!ok && threadIdx.x == 0) atomicExch(&g_ns_status, (int)LF_ERR_TIMEOUT);
 }
 
 size_t tc_smem_bytes() { return 6 * (size_t)kOpBytes + sizeof(NsShared) + 1024; }
@@ -1063,6 +1149,13 @@ extern "C" int lf_newton_inverse_residual(const void* a, const void* x, void* re
         return check_launch("ns_residual_kernel");
     });
     return LF_OK;
+}
+
+extern "C" int lf_selftest_bounded_wait(int timeout_ms, lf_stream_t stream) {
+    clear_error();
+    if (timeout_ms < 1 || timeout_ms > 10000) { set_error("timeout_ms must be in [1, 10000]"); return LF_ERR_INVALID; }
+    bounded_wait_probe_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>((uint64_t)timeout_ms * 1000000ull);
+    return check_launch("bounded_wait_probe_kernel");
 }
 
 // Synchronises the current device and returns (and optionally clears) the

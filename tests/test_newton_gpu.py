@@ -194,3 +194,19 @@ def test_against_reference_module(cuda, ref_module):
         assert np.all(np.abs(r_gpu - r_ref) <= 1e-4), (n, r_gpu, r_ref)
         torch.testing.assert_close(X, Xr, rtol=0, atol=1e-4 * Xr.abs().max().item())
         torch.testing.assert_close(d, dr, rtol=0, atol=1e-5 * dr.abs().max().item())
+
+
+def test_bounded_wait_reports_timeout(cuda):
+    # A device wait that nothing completes gives up after its limit and
+    # reports LF_ERR_TIMEOUT through the status word; the context stays usable.
+    assert capi.device_status(clear=True) in (0, capi.LF_ERR_TIMEOUT)
+    assert capi.device_status() == 0
+    s = torch.cuda.current_stream(cuda).cuda_stream
+    assert capi.lib().lf_selftest_bounded_wait(50, s) == capi.LF_OK
+    assert capi.device_status(clear=True) == capi.LF_ERR_TIMEOUT
+    assert capi.device_status() == 0
+    # still usable afterwards
+    A = spd(2, 64, seed=1).to(cuda)
+    X = capi.newton_inverse_fwd(A, 10)
+    torch.cuda.synchronize()
+    assert torch.isfinite(X).all()
