@@ -163,15 +163,29 @@ lsub_fwd_kernel(const T* __restrict__ q, const T* __restrict__ kT, T* __restrict
 #pragma unroll
         for (int r = 0; r < TM; ++r) {
             int64_t row = row0 + (int64_t)kThreads * r;
-#pragma unroll
-            for (int x = 0; x < DR / 16; ++x) {
-                A(&dst)[16] = *reinterpret_cast<A(*)[16]>(&qr[r][16 * x]);
-                const int valid = d - dc - 16 * x;
-                if (row < n && valid > 0) {
-                    load_chunk16<T>(Qb + row * d + dc + 16 * x, valid, vec, dst);
+            if constexpr (DR == 8) {
+                const int valid = d - dc;
+                if (row < n && valid >= 8 && vec && sizeof(T) == 4) {
+                    const float4* p = reinterpret_cast<const float4*>(Qb + row * d + dc);
+                    float4 x0 = __ldg(p), x1 = __ldg(p + 1);
+                    qr[r][0] = x0.x; qr[r][1] = x0.y; qr[r][2] = x0.z; qr[r][3] = x0.w;
+                    qr[r][4] = x1.x; qr[r][5] = x1.y; qr[r][6] = x1.z; qr[r][7] = x1.w;
                 } else {
 #pragma unroll
-                    for (int e = 0; e < 16; ++e) dst[e] = A(0);
+                    for (int e = 0; e < 8; ++e)
+                        qr[r][e] = (row < n && e < valid) ? Elem<T>::load(Qb[row * d + dc + e]) : A(0);
+                }
+            } else {
+#pragma unroll
+                for (int x = 0; x < DR / 16; ++x) {
+                    A(&dst)[16] = *reinterpret_cast<A(*)[16]>(&qr[r][16 * x]);
+                    const int valid = d - dc - 16 * x;
+                    if (row < n && valid > 0) {
+                        load_chunk16<T>(Qb + row * d + dc + 16 * x, valid, vec, dst);
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 16; ++e) dst[e] = A(0);
+                    }
                 }
             }
         }
@@ -294,27 +308,6 @@ int launch_fwd(const void* q, const void* kT, void* s, int64_t bh, int64_t n, in
     } else {
         if (d <= 16) return launch_fwd_dr<T, 16>(Q, K, S, bh, n, m, d, st);
         if (d <= 32) {
-            static const int variant = [] { const char* e = getenv("LFB_FWD_VARIANT"); return e ? atoi(e) : 0; }();
-            if (variant == 4) {
-                switch (pick_mc(m)) {
-                    case 4: return launch_fwd_mc<T, 4, 4, 16>(Q, K, S, bh, n, m, d, st);
-                    case 5: return launch_fwd_mc<T, 4, 5, 16>(Q, K, S, bh, n, m, d, st);
-                    case 6: return launch_fwd_mc<T, 4, 6, 16>(Q, K, S, bh, n, m, d, st);
-                    case 7: return launch_fwd_mc<T, 4, 7, 16>(Q, K, S, bh, n, m, d, st);
-                    default: return launch_fwd_mc<T, 4, 8, 16>(Q, K, S, bh, n, m, d, st);
-                }
-            }
-            if (variant == 5) return launch_fwd_mc<T, 1, 4, 32>(Q, K, S, bh, n, m, d, st);
-            if (variant == 6) return launch_fwd_mc<T, 1, 5, 32>(Q, K, S, bh, n, m, d, st);
-            if (variant == 2) {
-                switch (pick_mc(m)) {
-                    case 4: return launch_fwd_mc<T, 2, 4, 16>(Q, K, S, bh, n, m, d, st);
-                    case 5: return launch_fwd_mc<T, 2, 5, 16>(Q, K, S, bh, n, m, d, st);
-                    case 6: return launch_fwd_mc<T, 2, 6, 16>(Q, K, S, bh, n, m, d, st);
-                    case 7: return launch_fwd_mc<T, 2, 7, 16>(Q, K, S, bh, n, m, d, st);
-                    default: return launch_fwd_mc<T, 2, 8, 16>(Q, K, S, bh, n, m, d, st);
-                }
-            }
             return launch_fwd_dr<T, 32>(Q, K, S, bh, n, m, d, st);
         }
         if (d <= 64) return launch_fwd_dr<T, 64>(Q, K, S, bh, n, m, d, st);
