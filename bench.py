@@ -215,6 +215,8 @@ def run_b200(args, rank, world, dev):
     s = torch.empty(B, H, N, M, device=dev, dtype=dtype)
     dq = torch.empty_like(q)
     dk = torch.empty_like(kT)
+    ws_bytes = capi.laplace_sub_bwd_workspace_size(q, kT)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes else None
 
     ev_f = []
     ev_b = []
@@ -226,7 +228,7 @@ def run_b200(args, rank, world, dev):
         a.record(stream)
         capi.laplace_sub_fwd(q, kT, s)
         m_.record(stream)
-        capi.laplace_sub_bwd(ds, q, kT, dq, dk)
+        capi.laplace_sub_bwd(ds, q, kT, dq, dk, workspace=ws)
         e.record(stream)
         ev_f.append((a, m_))
         ev_b.append((m_, e))
@@ -251,7 +253,7 @@ def run_b200(args, rank, world, dev):
     clock_mhz = clk.summary()["sm_mhz"] or peaks.get("sm_max_mhz", 1965.0)
     issue_peak = sm_count * 4 * 32 * clock_mhz * 1e6  # thread-instructions/s at the sampled clock
     roofline = {
-        "bound": "hbm", "kernel": "lsub_bwd_kernel (fused dQ + dK^T)",
+        "bound": "hbm", "kernel": "lsub_bwd_fast_kernel balanced (fused dQ + dK^T) + lsub_bwd_dk_finalize",
         "achieved": bb / (bwd_ms / 1e3) / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
         "frac": bb / (bwd_ms / 1e3) / 1e9 / peaks["hbm_gbs"], "traffic": None,
         "peak_kind": peak_kind,
@@ -302,7 +304,7 @@ def run_b200(args, rank, world, dev):
         "e2e": {"value": world * dists / (e2e_ms / 1e3) / 1e9, "unit": UNIT, "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "api": "laplacianformer_b200.streaming.HostPipeline (C ABI, 8 B*H chunks on copy-in / kernel / copy-out streams) with pinned host buffers"},
-        "gpu_launches": 2 * args.steps,
+        "gpu_launches": (3 if ws is not None else 2) * args.steps,
         "clocks": clk.summary(),
     }
     if not args.skip_newton:
@@ -457,10 +459,12 @@ def run_only(args, dev):
         q, kT, ds = w["q"], w["kT"], w["ds"]
         s = torch.empty(q.shape[0], q.shape[1], q.shape[2], kT.shape[3], device=dev, dtype=dtype)
         dq, dk = torch.empty_like(q), torch.empty_like(kT)
+        ws_bytes = capi.laplace_sub_bwd_workspace_size(q, kT)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev) if ws_bytes else None
 
         def step():
             capi.laplace_sub_fwd(q, kT, s)
-            capi.laplace_sub_bwd(ds, q, kT, dq, dk)
+            capi.laplace_sub_bwd(ds, q, kT, dq, dk, workspace=ws)
     else:
         A = workloads.config3(device=dev, batch=args.ns_batch)["A"]
         X = torch.empty_like(A)

@@ -21,6 +21,7 @@
 #ifndef LAPLACIAN_B200_H
 #define LAPLACIAN_B200_H
 
+#include <stddef.h>
 #include <stdint.h>
 
 #if defined(__GNUC__)
@@ -118,6 +119,28 @@ LF_API int lf_laplace_sub_bwd(const void* g, const void* q, const void* kT,
                        void* dq, void* dkT,
                        int64_t bh, int64_t n, int64_t m, int64_t d,
                        int dtype, lf_stream_t stream);
+
+/* Device workspace bytes that lf_laplace_sub_bwd_ws takes for this shape on
+   the current device (it depends on the SM count); 0 when the shape runs
+   without workspace (d > 32, m > 64 or F64).  No counterpart in the
+   reference. */
+LF_API size_t lf_laplace_sub_bwd_workspace_size(int64_t bh, int64_t n, int64_t m, int64_t d, int dtype);
+
+/* lf_laplace_sub_bwd (both gradients) with the row chunks of all (b,h)
+   spread evenly over every SM: each CTA takes a contiguous run of 64-row
+   chunks that may cross (b,h) boundaries, and the dKT partials of the (b,h)
+   shared by several CTAs meet in `workspace` (16-byte aligned device memory
+   of at least lf_laplace_sub_bwd_workspace_size bytes; nothing in it needs
+   to be initialised), summed by a second kernel in a fixed order.  When the
+   size query gives 0, or dq or dkT is NULL, this is lf_laplace_sub_bwd and
+   the workspace is not touched.  Concurrent calls need distinct workspaces.
+   No counterpart in the reference, which splits rows with atomicAdd into a
+   zeroed output (src/LaplaceSubtraction_cuda_kernel.cu:568-580). */
+LF_API int lf_laplace_sub_bwd_ws(const void* g, const void* q, const void* kT,
+                          void* dq, void* dkT,
+                          int64_t bh, int64_t n, int64_t m, int64_t d,
+                          int dtype, void* workspace, size_t workspace_bytes,
+                          lf_stream_t stream);
 
 /* Legacy forward with the reference's per-output tree reduction in the
    storage type, including its behaviour for d that is not a power of two.

@@ -36,6 +36,8 @@ SIGNATURES = {
     "lf_laplace_sub_bwd_query": (_I, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I, _P]),
     "lf_laplace_sub_bwd_key": (_I, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I, _P]),
     "lf_laplace_sub_bwd": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I, _P]),
+    "lf_laplace_sub_bwd_workspace_size": (ctypes.c_size_t, [_I64, _I64, _I64, _I64, _I]),
+    "lf_laplace_sub_bwd_ws": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I, _P, ctypes.c_size_t, _P]),
     "lf_laplace_sub_reduce_fwd": (_I, [_P, _P, _P, _I64, _I64, _I64, _I64, _I, _P]),
     "lf_newton_inverse_supported": (_I, [_I64]),
     "lf_newton_inverse_fwd": (_I, [_P, _P, _I64, _I64, _I, _I, _P]),
@@ -116,8 +118,18 @@ def laplace_sub_fwd(q, kT, out=None):
     return out
 
 
-def laplace_sub_bwd(g, q, kT, dq=True, dk=True):
-    """Fused backward; dq/dk may be tensors, True (allocate) or None/False (skip)."""
+def laplace_sub_bwd_workspace_size(q, kT):
+    """Bytes of device workspace the balanced fused backward takes for this shape (0: none)."""
+    bh, n, m, d = _dims(q, kT)
+    return int(lib().lf_laplace_sub_bwd_workspace_size(bh, n, m, d, dtype_code(q)))
+
+
+def laplace_sub_bwd(g, q, kT, dq=True, dk=True, workspace=None):
+    """Fused backward; dq/dk may be tensors, True (allocate) or None/False (skip).
+
+    With both gradients and a shape that has a workspace size, the balanced
+    kernel runs on `workspace` (a uint8 device tensor; allocated here when
+    None); otherwise the workspace-free kernel runs."""
     _need_cuda(g, q, kT)
     bh, n, m, d = _dims(q, kT)
     if dq is True:
@@ -127,6 +139,14 @@ def laplace_sub_bwd(g, q, kT, dq=True, dk=True):
     dq = dq if isinstance(dq, torch.Tensor) else None
     dk = dk if isinstance(dk, torch.Tensor) else None
     _need_cuda(dq, dk)
+    need = laplace_sub_bwd_workspace_size(q, kT) if (dq is not None and dk is not None) else 0
+    if need:
+        if workspace is None:
+            workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+        _check(lib().lf_laplace_sub_bwd_ws(_ptr(g), _ptr(q), _ptr(kT), _ptr(dq), _ptr(dk), bh, n, m, d,
+                                           dtype_code(q), _ptr(workspace), workspace.numel() * workspace.element_size(),
+                                           _stream(q)), "lf_laplace_sub_bwd_ws")
+        return dq, dk
     _check(lib().lf_laplace_sub_bwd(_ptr(g), _ptr(q), _ptr(kT), _ptr(dq), _ptr(dk), bh, n, m, d, dtype_code(q),
                                     _stream(q)), "lf_laplace_sub_bwd")
     return dq, dk

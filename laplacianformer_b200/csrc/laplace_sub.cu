@@ -134,13 +134,17 @@ __device__ __forceinline__ void accum_chunk(A (&acc)[TM][MC], const A (&qr)[TM][
 template <typename T, int TM, int MC, int DR>
 __global__ void __launch_bounds__(kThreads)
 lsub_fwd_kernel(const T* __restrict__ q, const T* __restrict__ kT, T* __restrict__ s,
-                int n, int m, int d, int tiles_per_bh, bool vec) {
+                int n, int m, int d, int tiles_per_bh, bool vec, bool stage_out) {
     using A = typename Elem<T>::acc;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     A* ks = reinterpret_cast<A*>(smem_raw);
     const int d16 = (d + 15) & ~15;
     const int DP = d16 > DR ? ((d + DR - 1) / DR) * DR : DR;
     const int MP = ((m + MC - 1) / MC) * MC;
+    // Output tile [kThreads*TM][m] in the storage type, after ks (16-byte
+    // aligned); written row-wise by the lanes, copied out as one contiguous
+    // run of S with 16-byte stores.
+    T* so = reinterpret_cast<T*>(smem_raw + (((size_t)MP * DP * sizeof(A) + 15) & ~(size_t)15));
     const bool single = d <= DR;
 
     const int bh = blockIdx.x / tiles_per_bh;
@@ -210,6 +214,13 @@ lsub_fwd_kernel(const T* __restrict__ q, const T* __restrict__ kT, T* __restrict
         }
 #pragma unroll
         for (int r = 0; r < TM; ++r) {
+            if (stage_out) {
+                T* out = so + (threadIdx.x + kThreads * r) * m + mc;
+#pragma unroll
+                for (int j = 0; j < MC; ++j)
+                    if (mc + j < m) out[j] = Elem<T>::store(acc[r][j]);
+                continue;
+            }
             int64_t row = row0 + (int64_t)kThreads * r;
             if (row >= n) continue;
             T* out = Sb + row * m + mc;
@@ -218,6 +229,23 @@ lsub_fwd_kernel(const T* __restrict__ q, const T* __restrict__ kT, T* __restrict
                 if (mc + j < m) out[j] = Elem<T>::store(acc[r][j]);
         }
     }
+    if (!stage_out) return;
+    __syncthreads();
+    // The tile's rows are contiguous in S: copy valid_rows*m elements.
+    const int64_t trow = (int64_t)tile * (kThreads * TM);
+    const int64_t rows = (n - trow) < (int64_t)(kThreads * TM) ? (n - trow) : (int64_t)(kThreads * TM);
+    const int64_t cnt = rows * m;
+    T* dst = Sb + trow * m;
+    constexpr int V = 16 / sizeof(T);
+    int64_t head = 0;
+    if ((reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+        const int64_t nv = cnt / V;
+        const uint4* src4 = reinterpret_cast<const uint4*>(so);
+        uint4* dst4 = reinterpret_cast<uint4*>(dst);
+        for (int64_t e = threadIdx.x; e < nv; e += kThreads) dst4[e] = src4[e];
+        head = nv * V;
+    }
+    for (int64_t e = head + threadIdx.x; e < cnt; e += kThreads) dst[e] = so[e];
 }
 
 // Landmark chunk per thread: the MC in 4..8 that pads m the least.
@@ -240,10 +268,28 @@ size_t fwd_smem(int64_t m, int64_t d) {
     return (size_t)MP * DP * sizeof(A);
 }
 
+// Bytes of the staged output tile, or 0 when S is stored directly (tiles
+// above kStageMax would cost occupancy).
+constexpr size_t kStageMax = 64 * 1024;
+template <typename T, int TM>
+size_t fwd_stage_bytes(int64_t m) {
+    size_t b = (size_t)kThreads * TM * m * sizeof(T);
+    return b <= kStageMax ? b : 0;
+}
+
+template <typename T, int TM, int MC, int DR>
+size_t fwd_smem_total(int64_t m, int64_t d) {
+    size_t st = fwd_stage_bytes<T, TM>(m);
+    size_t ks = fwd_smem<T, TM, MC, DR>(m, d);
+    return st ? ((ks + 15) & ~(size_t)15) + st : ks;
+}
+
 template <typename T, int TM, int MC, int DR>
 int launch_fwd_mc(const T* q, const T* kT, T* s, int64_t bh, int64_t n, int64_t m, int64_t d,
                   cudaStream_t st) {
-    size_t smem = fwd_smem<T, TM, MC, DR>(m, d);
+    size_t smem = fwd_smem_total<T, TM, MC, DR>(m, d);
+    const bool stage = fwd_stage_bytes<T, TM>(m) != 0 && smem <= (size_t)max_optin_smem();
+    if (!stage) smem = fwd_smem<T, TM, MC, DR>(m, d);
     if (smem > (size_t)max_optin_smem()) {
         set_error("LaplaceSubtraction forward: m*d = %lld*%lld needs %zu bytes of shared memory",
                   (long long)m, (long long)d, smem);
@@ -256,7 +302,7 @@ int launch_fwd_mc(const T* q, const T* kT, T* s, int64_t bh, int64_t n, int64_t 
     int64_t blocks = bh * tiles;
     if (blocks > 0x7fffffff) { set_error("too many blocks"); return LF_ERR_UNSUPPORTED; }
     bool vec = (d % 16 == 0) && aligned(q, 16);
-    kern<<<(unsigned)blocks, kThreads, smem, st>>>(q, kT, s, (int)n, (int)m, (int)d, tiles, vec);
+    kern<<<(unsigned)blocks, kThreads, smem, st>>>(q, kT, s, (int)n, (int)m, (int)d, tiles, vec, stage);
     return check_launch("lsub_fwd_kernel");
 }
 
@@ -266,16 +312,15 @@ int launch_fwd_mc(const T* q, const T* kT, T* s, int64_t bh, int64_t n, int64_t 
 template <typename T, int MC, int DR>
 int launch_fwd_tm(const T* Q, const T* K, T* S, int64_t bh, int64_t n, int64_t m, int64_t d, cudaStream_t st) {
     if constexpr (DR <= 32) {
-        const size_t smem = fwd_smem<T, 2, MC, DR>(m, d);
-        if (smem <= (size_t)max_optin_smem()) {
+        const size_t smem1 = fwd_smem_total<T, 1, MC, DR>(m, d);
+        const size_t smem2 = fwd_smem_total<T, 2, MC, DR>(m, d);
+        if (smem1 <= (size_t)max_optin_smem() && smem2 <= (size_t)max_optin_smem()) {
             auto k1 = lsub_fwd_kernel<T, 1, MC, DR>;
             auto k2 = lsub_fwd_kernel<T, 2, MC, DR>;
-            if (smem > 48 * 1024) {
-                cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-                cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            }
-            double e1 = wave_efficiency(bh * ((n + kThreads - 1) / kThreads), cta_slots(k1, smem));
-            double e2 = wave_efficiency(bh * ((n + 2 * kThreads - 1) / (2 * kThreads)), cta_slots(k2, smem));
+            if (smem1 > 48 * 1024) cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem1);
+            if (smem2 > 48 * 1024) cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem2);
+            double e1 = wave_efficiency(bh * ((n + kThreads - 1) / kThreads), cta_slots(k1, smem1));
+            double e2 = wave_efficiency(bh * ((n + 2 * kThreads - 1) / (2 * kThreads)), cta_slots(k2, smem2));
             if (e1 > e2 + 0.05) return launch_fwd_mc<T, 1, MC, DR>(Q, K, S, bh, n, m, d, st);
         }
         return launch_fwd_mc<T, 2, MC, DR>(Q, K, S, bh, n, m, d, st);
@@ -372,6 +417,10 @@ struct BwdGeom {
     int KSTR;         // row stride of the per-CTA dKT accumulator (odd, conflict free)
     int rows_per_cta;
     int RC;           // query rows staged per pass (<= kRowChunk)
+    // Balanced (flat) launch of the fast backward: the bh*U row chunks of
+    // kRowChunk rows (U = chunks per (b,h)) are dealt out as contiguous runs
+    // of P chunks per CTA.
+    int64_t U, P, total;
 };
 
 // grid = (cs, bh, channel groups), cluster = (cs, 1, 1).  CTA x of (b,h)
@@ -572,10 +621,18 @@ lsub_bwd_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* __res
 // shuffles, column sums stay in registers for the whole CTA, and the next
 // chunk's dS and Q are loaded into registers while the current one is being
 // consumed.  Same arithmetic and cluster reduction as lsub_bwd_kernel.
-template <typename T, int MB, bool DQ, bool DK>
+//
+// FLAT (both gradients only): no cluster; CTA i takes row chunks
+// [i*P, (i+1)*P) of the flattened (b,h, chunk) order, which may cross (b,h)
+// boundaries.  A (b,h) whose chunks all lie in one CTA gets its dKT written
+// directly; the partial dKT of a (b,h) shared by several CTAs goes to
+// workspace slot 2i (the CTA's first segment) or 2i+1 (its last), and
+// lsub_bwd_dk_finalize adds the slots.  Every CTA-slot of the machine works
+// (a per-(b,h) cluster leaves SMs idle when bh*cs is not a multiple of them).
+template <typename T, int MB, bool DQ, bool DK, bool FLAT>
 __global__ void __launch_bounds__(kThreads, 1)
 lsub_bwd_fast_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* __restrict__ kT,
-                     T* __restrict__ dq, T* __restrict__ dk, BwdGeom geo) {
+                     T* __restrict__ dq, T* __restrict__ dk, BwdGeom geo, float* __restrict__ ws) {
     using A = typename Elem<T>::acc;
     constexpr int RC = kRowChunk;   // 64 rows per chunk
     constexpr int CPT = MB / 4;     // landmarks per staging thread
@@ -591,15 +648,30 @@ lsub_bwd_fast_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* 
     A* cpart = dkb + CW * geo.KSTR;            // [8][MP]
     A* dpart = cpart + (kThreads / 32) * MP;   // [8][CW][KSTR] per-warp dKT partials
 
-    cg::cluster_group cluster = cg::this_cluster();
-    const int bh = blockIdx.y;
-    const int split = blockIdx.x;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int c = lane;                 // this lane's channel
     const bool lane_active = c < d;
     const int rg = warp;                // row group (8 warps)
     const int sr = tid >> 2, sq = tid & 3;
 
+    int64_t u = FLAT ? (int64_t)blockIdx.x * geo.P : 0;
+    const int64_t u_end = FLAT ? ((u + geo.P < geo.total) ? u + geo.P : geo.total) : 1;
+    for (int seg = 0; u < u_end; ++seg) {
+    int bh;
+    int64_t r_begin, r_end, u_next;
+    if constexpr (FLAT) {
+        bh = (int)(u / geo.U);
+        const int64_t ub = (int64_t)bh * geo.U;
+        u_next = (ub + geo.U < u_end) ? ub + geo.U : u_end;
+        r_begin = (u - ub) * kRowChunk;
+        r_end = (u_next - ub) * kRowChunk;
+        if (r_end > n) r_end = n;
+    } else {
+        bh = blockIdx.y;
+        r_begin = (int64_t)blockIdx.x * geo.rows_per_cta;
+        r_end = (r_begin + geo.rows_per_cta < (int64_t)n) ? r_begin + geo.rows_per_cta : (int64_t)n;
+        u_next = 1;
+    }
     const T* Gb = g + (int64_t)bh * n * m;
     const T* Qb = q + (int64_t)bh * n * d;
     const T* Kb = kT + (int64_t)bh * d * m;
@@ -614,9 +686,6 @@ lsub_bwd_fast_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* 
     A colp[CPT];
 #pragma unroll
     for (int k = 0; k < CPT; ++k) colp[k] = A(0);
-
-    const int64_t r_begin = (int64_t)split * geo.rows_per_cta;
-    const int64_t r_end = (r_begin + geo.rows_per_cta < (int64_t)n) ? r_begin + geo.rows_per_cta : (int64_t)n;
 
     A pg[CPT], pq[8];
     auto load_chunk = [&](int64_t rc) {
@@ -681,7 +750,7 @@ lsub_bwd_fast_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* 
         }
     }
 
-    if (!DK) return;
+    if (!DK) { u = u_next; continue; }
 
     // Column sums: reduce colp over the 8 rows of the warp that share a
     // quarter (lanes 4 apart), then across warps through shared memory.
@@ -711,8 +780,21 @@ lsub_bwd_fast_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* 
         int cc = e / m, j = e - cc * m;
         A sacc = csum[j];
         for (int w = 0; w < kThreads / 32; ++w) sacc += dpart[(w * CW + cc) * geo.KSTR + j];
-        dkb[cc * geo.KSTR + j] = sacc;
+        if constexpr (FLAT) {
+            // Whole (b,h) in this CTA: final value; else a workspace slot.
+            const bool whole = (u == (int64_t)bh * geo.U) && (u_next == (int64_t)bh * geo.U + geo.U);
+            if (whole) dk[(int64_t)bh * d * m + e] = Elem<T>::store(sacc);
+            else ws[((int64_t)2 * blockIdx.x + (seg == 0 ? 0 : 1)) * d * m + e] = (float)sacc;
+        } else {
+            dkb[cc * geo.KSTR + j] = sacc;
+        }
     }
+    if constexpr (FLAT) {
+        __syncthreads();  // cpart/dpart/csum are reused by the next segment
+        u = u_next;
+        continue;
+    } else {
+    cg::cluster_group cluster = cg::this_cluster();
     cluster.sync();
     const int cs = (int)cluster.num_blocks();
     const int rank = (int)cluster.block_rank();
@@ -730,6 +812,29 @@ lsub_bwd_fast_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* 
         dkout[e] = Elem<T>::store(sacc);
     }
     cluster.sync();
+    u = u_next;
+    }
+    }  // segments
+}
+
+// dKT of every (b,h) that the flat backward split over several CTAs: the
+// sum of their workspace slots in CTA order (bitwise reproducible).
+template <typename T>
+__global__ void __launch_bounds__(kThreads)
+lsub_bwd_dk_finalize(const float* __restrict__ ws, T* __restrict__ dk, int d, int m, int64_t U, int64_t P) {
+    const int64_t b = blockIdx.x;
+    const int64_t first = b * U, last = b * U + U - 1;
+    const int64_t c0 = first / P, c1 = last / P;
+    if (c0 == c1) return;
+    const int64_t dm = (int64_t)d * m;
+    for (int64_t e = threadIdx.x; e < dm; e += kThreads) {
+        float acc = 0.0f;
+        for (int64_t c = c0; c <= c1; ++c) {
+            const int64_t slot = 2 * c + (c * P >= first ? 0 : 1);
+            acc += ws[slot * dm + e];
+        }
+        dk[b * dm + e] = Elem<T>::store(acc);
+    }
 }
 
 template <typename T, int MB, bool DQ, bool DK>
@@ -743,7 +848,7 @@ int launch_bwd_fast(const T* g, const T* q, const T* kT, T* dq, T* dk, int64_t b
     size_t smem = sizeof(A) * ((size_t)kRowChunk * MB + (size_t)kRowChunk * 32 + kRowChunk + MB +
                                (size_t)32 * geo.KSTR + (size_t)(kThreads / 32) * MB +
                                (DK ? (size_t)(kThreads / 32) * 32 * geo.KSTR : 0));
-    auto kern = lsub_bwd_fast_kernel<T, MB, DQ, DK>;
+    auto kern = lsub_bwd_fast_kernel<T, MB, DQ, DK, false>;
     if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     const int64_t slots = cta_slots(kern, smem);
     const int64_t max_by_rows = (n + kRowChunk - 1) / kRowChunk;
@@ -769,12 +874,76 @@ int launch_bwd_fast(const T* g, const T* q, const T* kT, T* dq, T* dk, int64_t b
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t err = cudaLaunchKernelEx(&cfg, kern, g, q, kT, dq, dk, geo);
+    cudaError_t err = cudaLaunchKernelEx(&cfg, kern, g, q, kT, dq, dk, geo, (float*)nullptr);
     if (err != cudaSuccess) {
         set_error("lsub_bwd_fast_kernel launch: %s", cudaGetErrorString(err));
         return LF_ERR_CUDA;
     }
     return check_launch("lsub_bwd_fast_kernel");
+}
+
+// Balanced launch of the fast backward (both gradients).  With ws == nullptr
+// only computes the workspace bytes into *need (0: this shape does not take
+// the flat path).  Returns LF_OK, or an error when ws is given but smaller
+// than needed.
+template <typename T, int MB>
+int launch_bwd_flat(const T* g, const T* q, const T* kT, T* dq, T* dk, int64_t bh, int64_t n, int64_t m,
+                    int64_t d, float* ws, size_t ws_bytes, size_t* need, cudaStream_t st) {
+    using A = typename Elem<T>::acc;
+    BwdGeom geo;
+    geo.n = (int)n; geo.m = (int)m; geo.d = (int)d;
+    geo.DBC = 1; geo.MCN = 1; geo.RG = kThreads / 32; geo.MP = MB; geo.RC = kRowChunk;
+    geo.KSTR = (int)(m | 1);
+    geo.rows_per_cta = 0;
+    size_t smem = sizeof(A) * ((size_t)kRowChunk * MB + (size_t)kRowChunk * 32 + kRowChunk + MB +
+                               (size_t)32 * geo.KSTR + (size_t)(kThreads / 32) * MB +
+                               (size_t)(kThreads / 32) * 32 * geo.KSTR);
+    auto kern = lsub_bwd_fast_kernel<T, MB, true, true, true>;
+    if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    const int64_t slots = cta_slots(kern, smem);
+    geo.U = (n + kRowChunk - 1) / kRowChunk;
+    geo.total = bh * geo.U;
+    geo.P = (geo.total + slots - 1) / slots;
+    const int64_t grid = (geo.total + geo.P - 1) / geo.P;
+    const size_t bytes = (size_t)2 * grid * d * m * sizeof(float);
+    if (need) *need = bytes;
+    if (!ws) return LF_OK;
+    if (ws_bytes < bytes) {
+        set_error("LaplaceSubtraction backward: workspace of %zu bytes, %zu needed", ws_bytes, bytes);
+        return LF_ERR_INVALID;
+    }
+    kern<<<(unsigned)grid, kThreads, smem, st>>>(g, q, kT, dq, dk, geo, ws);
+    int rc = check_launch("lsub_bwd_fast_kernel");
+    if (rc) return rc;
+    if (bh > 0x7fffffff) { set_error("b*h too large"); return LF_ERR_UNSUPPORTED; }
+    lsub_bwd_dk_finalize<T><<<(unsigned)bh, kThreads, 0, st>>>(ws, dk, (int)d, (int)m, geo.U, geo.P);
+    return check_launch("lsub_bwd_dk_finalize");
+}
+
+template <typename T>
+int launch_bwd_flat_t(const void* g, const void* q, const void* kT, void* dq, void* dk, int64_t bh, int64_t n,
+                      int64_t m, int64_t d, void* ws, size_t ws_bytes, size_t* need, cudaStream_t st) {
+    if (need) *need = 0;
+    if constexpr (sizeof(T) == 8) {
+        return LF_OK;
+    } else {
+        if (!(d <= 32 && m <= 64)) return LF_OK;
+        const T* G = static_cast<const T*>(g);
+        const T* Q = static_cast<const T*>(q);
+        const T* K = static_cast<const T*>(kT);
+        T* DQp = static_cast<T*>(dq);
+        T* DKp = static_cast<T*>(dk);
+        float* W = static_cast<float*>(ws);
+        const int64_t m4 = (m + 3) & ~3;
+        switch (m4 <= 16 ? 16 : (m4 <= 32 ? 32 : (m4 <= 48 ? 48 : (m4 <= 52 ? 52 : (m4 <= 56 ? 56 : 64))))) {
+            case 16: return launch_bwd_flat<T, 16>(G, Q, K, DQp, DKp, bh, n, m, d, W, ws_bytes, need, st);
+            case 32: return launch_bwd_flat<T, 32>(G, Q, K, DQp, DKp, bh, n, m, d, W, ws_bytes, need, st);
+            case 48: return launch_bwd_flat<T, 48>(G, Q, K, DQp, DKp, bh, n, m, d, W, ws_bytes, need, st);
+            case 52: return launch_bwd_flat<T, 52>(G, Q, K, DQp, DKp, bh, n, m, d, W, ws_bytes, need, st);
+            case 56: return launch_bwd_flat<T, 56>(G, Q, K, DQp, DKp, bh, n, m, d, W, ws_bytes, need, st);
+            default: return launch_bwd_flat<T, 64>(G, Q, K, DQp, DKp, bh, n, m, d, W, ws_bytes, need, st);
+        }
+    }
 }
 
 // Wide variant of the fused backward: d <= 64 and m <= 256 (configuration 5:
@@ -1278,6 +1447,38 @@ extern "C" int lf_laplace_sub_bwd(const void* g, const void* q, const void* kT, 
                                   lf_stream_t stream) {
     clear_error();
     return bwd_common(g, q, kT, dq, dkT, bh, n, m, d, dtype, stream);
+}
+
+// Workspace bytes of lf_laplace_sub_bwd_ws for this shape (0: the shape
+// runs without workspace).  Depends on the current device's SM count.
+extern "C" size_t lf_laplace_sub_bwd_workspace_size(int64_t bh, int64_t n, int64_t m, int64_t d, int dtype) {
+    clear_error();
+    if (bh <= 0 || n <= 0 || m <= 0 || d <= 0) return 0;
+    if (dtype < LF_F32 || dtype > LF_BF16) { set_error("unsupported dtype code %d", dtype); return 0; }
+    size_t need = 0;
+    LF_DISPATCH(dtype, T, {
+        launch_bwd_flat_t<T>(nullptr, nullptr, nullptr, nullptr, nullptr, bh, n, m, d, nullptr, 0, &need, 0);
+        return need;
+    });
+    return 0;
+}
+
+extern "C" int lf_laplace_sub_bwd_ws(const void* g, const void* q, const void* kT, void* dq, void* dkT,
+                                     int64_t bh, int64_t n, int64_t m, int64_t d, int dtype, void* workspace,
+                                     size_t workspace_bytes, lf_stream_t stream) {
+    clear_error();
+    const size_t need = lf_laplace_sub_bwd_workspace_size(bh, n, m, d, dtype);
+    if (need == 0 || !dq || !dkT) return bwd_common(g, q, kT, dq, dkT, bh, n, m, d, dtype, stream);
+    int rc = check_args(g, q, kT, bh, n, m, d, dtype);
+    if (rc) return rc;
+    if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 15)) {
+        set_error("LaplaceSubtraction backward: workspace must be a 16-byte aligned device pointer");
+        return LF_ERR_INVALID;
+    }
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    LF_DISPATCH(dtype, T, return launch_bwd_flat_t<T>(g, q, kT, dq, dkT, bh, n, m, d, workspace, workspace_bytes,
+                                                      nullptr, st));
+    return LF_OK;
 }
 
 extern "C" int lf_laplace_sub_bwd_query(const void* g, const void* q, const void* kT, void* dq,

@@ -120,6 +120,19 @@ void LaplaceSubtraction_backward_cuda(const at::Tensor gradOutput, const at::Ten
     c10::cuda::CUDAGuard guard(query.device());
     at::Tensor g = gradOutput.contiguous();
     Dims s = dims_of(query, key);
+    if (gradQuery.defined() && gradKey.defined()) {
+        // Balanced kernel when the shape has one: its workspace comes from
+        // the caching allocator on the op's stream.
+        const size_t need = lf_laplace_sub_bwd_workspace_size(s.bh, s.n, s.m, s.d, dtype_code(query));
+        if (need) {
+            at::Tensor ws = at::empty({(int64_t)need}, query.options().dtype(at::kByte));
+            raise_on(lf_laplace_sub_bwd_ws(g.data_ptr(), query.data_ptr(), key.data_ptr(), gradQuery.data_ptr(),
+                                           gradKey.data_ptr(), s.bh, s.n, s.m, s.d, dtype_code(query), ws.data_ptr(),
+                                           need, stream_of(query)),
+                     "LaplaceSubtraction_backward");
+            return;
+        }
+    }
     raise_on(lf_laplace_sub_bwd(g.data_ptr(), query.data_ptr(), key.data_ptr(),
                                 gradQuery.defined() ? gradQuery.data_ptr() : nullptr,
                                 gradKey.defined() ? gradKey.data_ptr() : nullptr, s.bh, s.n, s.m, s.d,
