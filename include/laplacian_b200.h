@@ -142,6 +142,30 @@ LF_API int lf_laplace_sub_bwd_ws(const void* g, const void* q, const void* kT,
                           int dtype, void* workspace, size_t workspace_bytes,
                           lf_stream_t stream);
 
+/* Size of the fixed device scratch of lf_laplace_sub_bwd_noalloc. */
+#define LF_BWD_NOALLOC_SCRATCH_BYTES (2u << 20)
+
+/* lf_laplace_sub_bwd_ws for callers that cannot allocate device memory: code
+   running where cudaMalloc is not allowed or not wanted (inside a custom
+   allocator or memory-pool callback, a host that has handed all device memory
+   to its own pool, or a real-time loop that must not synchronise, which
+   cudaMalloc/cudaFree can do).  Its workspace is a fixed 2 MiB array
+   (LF_BWD_NOALLOC_SCRATCH_BYTES) compiled into the library, which every GPU
+   that loads the library holds until the process exits; nothing is allocated
+   per call.  Both dq and dkT are required.  Shapes whose
+   lf_laplace_sub_bwd_workspace_size exceeds 2 MiB are rejected with
+   LF_ERR_UNSUPPORTED; shapes with size 0 run lf_laplace_sub_bwd.  The first
+   call on a device looks up the array's device address (cudaGetSymbolAddress)
+   with that device current; make that first call before any stream capture.
+   All calls share the one array and each overwrites what it reads (nothing
+   needs to start at zero), so calls that can overlap on the GPU (different
+   streams or host threads) race: serialise them.  No counterpart in the
+   reference. */
+LF_API int lf_laplace_sub_bwd_noalloc(const void* g, const void* q, const void* kT,
+                               void* dq, void* dkT,
+                               int64_t bh, int64_t n, int64_t m, int64_t d,
+                               int dtype, lf_stream_t stream);
+
 /* Legacy forward with the reference's per-output tree reduction in the
    storage type, including its behaviour for d that is not a power of two.
    Replaces laplace::LaplaceSubtraction_reduce_forward_cuda

@@ -27,6 +27,8 @@
 #include <cooperative_groups.h>
 #include <stdlib.h>
 
+#include <mutex>
+
 #include "lf_common.cuh"
 
 namespace cg = cooperative_groups;
@@ -1478,6 +1480,67 @@ extern "C" int lf_laplace_sub_bwd_ws(const void* g, const void* q, const void* k
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     LF_DISPATCH(dtype, T, return launch_bwd_flat_t<T>(g, q, kT, dq, dkT, bh, n, m, d, workspace, workspace_bytes,
                                                       nullptr, st));
+    return LF_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Fused backward without any allocation
+// ---------------------------------------------------------------------------
+// Scratch of lf_laplace_sub_bwd_noalloc: the dKT partial slots of the
+// balanced backward.  A file-scope device array, so it exists on every GPU
+// that loads this library from load until process exit, and no call has to
+// allocate.  Every call overwrites the slots it later reads, so nothing in
+// it has to start at zero; all calls share it, so calls that can overlap on
+// the GPU (other streams, other host threads) race on it.
+constexpr size_t kNoAllocScratchBytes = (size_t)2 << 20;  // 2 MiB
+static __device__ __align__(256) float g_bwd_scratch[kNoAllocScratchBytes / sizeof(float)];
+
+namespace {
+constexpr int kNoAllocMaxDev = 64;
+std::once_flag g_scratch_once[kNoAllocMaxDev];
+void* g_scratch_ptr[kNoAllocMaxDev];
+cudaError_t g_scratch_err[kNoAllocMaxDev];
+
+// In host code g_bwd_scratch names a host-side stand-in; the device address
+// is asked for once per device, with that device current.
+void scratch_setup(int dev) {
+    void* p = nullptr;
+    g_scratch_err[dev] = cudaGetSymbolAddress(&p, g_bwd_scratch);
+    g_scratch_ptr[dev] = (g_scratch_err[dev] == cudaSuccess) ? p : nullptr;
+}
+}  // namespace
+
+extern "C" int lf_laplace_sub_bwd_noalloc(const void* g, const void* q, const void* kT, void* dq, void* dkT,
+                                          int64_t bh, int64_t n, int64_t m, int64_t d, int dtype,
+                                          lf_stream_t stream) {
+    clear_error();
+    if ((!dq && bh * n * d > 0) || (!dkT && bh * d * m > 0)) {
+        set_error("lf_laplace_sub_bwd_noalloc computes both gradients: dq and dkT must be given");
+        return LF_ERR_INVALID;
+    }
+    const size_t need = lf_laplace_sub_bwd_workspace_size(bh, n, m, d, dtype);
+    if (need == 0) return bwd_common(g, q, kT, dq, dkT, bh, n, m, d, dtype, stream);  // no scratch needed
+    if (need > kNoAllocScratchBytes) {
+        set_error("lf_laplace_sub_bwd_noalloc: this shape needs %zu bytes of scratch, more than its fixed %zu "
+                  "(use lf_laplace_sub_bwd_ws or lf_laplace_sub_bwd)", need, kNoAllocScratchBytes);
+        return LF_ERR_UNSUPPORTED;
+    }
+    int rc = check_args(g, q, kT, bh, n, m, d, dtype);
+    if (rc) return rc;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDev) {
+        set_error("lf_laplace_sub_bwd_noalloc: no usable current device");
+        return LF_ERR_CUDA;
+    }
+    std::call_once(g_scratch_once[dev], scratch_setup, dev);
+    if (!g_scratch_ptr[dev]) {
+        set_error("lf_laplace_sub_bwd_noalloc: cudaGetSymbolAddress failed: %s",
+                  cudaGetErrorString(g_scratch_err[dev]));
+        return LF_ERR_CUDA;
+    }
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    LF_DISPATCH(dtype, T, return launch_bwd_flat_t<T>(g, q, kT, dq, dkT, bh, n, m, d, g_scratch_ptr[dev],
+                                                      kNoAllocScratchBytes, nullptr, st));
     return LF_OK;
 }
 

@@ -1,0 +1,69 @@
+"""lf_laplace_sub_bwd_noalloc: the fused LaplaceSubtraction backward for
+callers that may not allocate device memory (allocator callbacks, hosts
+whose device memory is owned by their own pool, loops that must not
+synchronise).  It uses a fixed scratch array inside the library, so these
+checks call it through the C ABI and compare with lf_laplace_sub_bwd on two
+calls in a row: the second call must not be disturbed by what the first left
+in the shared scratch.  Collected last on purpose."""
+import numpy as np
+import pytest
+import torch
+
+from laplacianformer_b200 import capi
+
+pytestmark = pytest.mark.gpu
+
+SCRATCH = 2 << 20
+TOL = {torch.float32: 1e-5, torch.float16: 1e-2, torch.bfloat16: 1e-2}
+
+
+def _inputs(shape, dtype, seed):
+    B, H, N, D, M = shape
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(B, H, N, D, generator=g).to(dtype).cuda()
+    k = torch.randn(B, H, D, M, generator=g).to(dtype).cuda()
+    gr = torch.randn(B, H, N, M, generator=g).to(dtype).cuda()
+    return gr, q, k
+
+
+def _call(fn, g, q, k):
+    dq, dk = torch.empty_like(q), torch.empty_like(k)
+    bh, n, m, d = q.shape[0] * q.shape[1], q.shape[2], k.shape[3], q.shape[3]
+    rc = fn(g.data_ptr(), q.data_ptr(), k.data_ptr(), dq.data_ptr(), dk.data_ptr(), bh, n, m, d,
+            capi.dtype_code(q), None)
+    return rc, dq, dk
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16], ids=str)
+def test_noalloc_matches_existing_backward_twice(dtype):
+    L = capi.lib()
+    shapes = [(4, 2, 3136, 32, 49), (8, 40, 64, 32, 49)]
+    for call, (shape, seed) in enumerate(zip(shapes, (11, 12))):
+        g, q, k = _inputs(shape, dtype, seed)
+        assert 0 < L.lf_laplace_sub_bwd_workspace_size(q.shape[0] * q.shape[1], q.shape[2], k.shape[3],
+                                                       q.shape[3], capi.dtype_code(q)) <= SCRATCH
+        rc, dq, dk = _call(L.lf_laplace_sub_bwd_noalloc, g, q, k)
+        assert rc == capi.LF_OK, L.lf_last_error()
+        rc, rq, rk = _call(L.lf_laplace_sub_bwd, g, q, k)
+        assert rc == capi.LF_OK
+        torch.cuda.synchronize()
+        ga = g.double().abs()
+        row = ga.sum(-1, keepdim=True)
+        col = ga.sum(-2).unsqueeze(-2)
+        assert torch.all((dq.double() - rq.double()).abs() <= TOL[dtype] * row), f"dQ, call {call + 1}"
+        assert torch.all((dk.double() - rk.double()).abs() <= TOL[dtype] * col), f"dK, call {call + 1}"
+
+
+def test_noalloc_rejects_shapes_beyond_its_scratch():
+    L = capi.lib()
+    g, q, k = _inputs((2, 2, 70, 32, 64), torch.float32, 0)
+    for bh in (4096, 65536):
+        need = L.lf_laplace_sub_bwd_workspace_size(bh, 3136, 64, 32, capi.LF_F32)
+        if need > SCRATCH:
+            # sizes only: the check fails before any pointer is used
+            rc = L.lf_laplace_sub_bwd_noalloc(g.data_ptr(), q.data_ptr(), k.data_ptr(), q.data_ptr(),
+                                              k.data_ptr(), bh, 3136, 64, 32, capi.LF_F32, None)
+            assert rc == capi.LF_ERR_UNSUPPORTED
+            assert b"scratch" in L.lf_last_error()
+            return
+    pytest.skip("no shape on this device needs more than the fixed scratch")
