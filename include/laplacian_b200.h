@@ -166,6 +166,27 @@ LF_API int lf_laplace_sub_bwd_noalloc(const void* g, const void* q, const void* 
                                int64_t bh, int64_t n, int64_t m, int64_t d,
                                int dtype, lf_stream_t stream);
 
+/* Device buffer bytes lf_laplace_sub_fwd_bwd_host needs for this shape and
+   chunk count (three rotating sets of per-chunk operands, results and
+   backward workspace).  No counterpart in the reference. */
+LF_API size_t lf_laplace_sub_host_buffer_size(int64_t bh, int64_t n, int64_t m, int64_t d, int dtype,
+                                       int chunks);
+
+/* Forward S and both gradients dQ, dKT for operands in HOST memory (pinned,
+   for the copies to overlap): q, kT, g are read and s, dq, dkT written in
+   host memory.  The bh slices are cut into `chunks` pieces that stream
+   through host-to-device copies, the kernels and device-to-host copies on
+   three library-owned streams, so both PCIe directions and the kernels
+   overlap.  `dbuf` is a 256-byte aligned device buffer of at least
+   lf_laplace_sub_host_buffer_size bytes.  Asynchronous: `stream` waits for
+   the last copy-out (synchronise it before reading the host results).  The
+   first call on a device creates its streams and events.  No counterpart in
+   the reference, whose operators take device tensors only. */
+LF_API int lf_laplace_sub_fwd_bwd_host(const void* q, const void* kT, const void* g,
+                                void* s, void* dq, void* dkT,
+                                int64_t bh, int64_t n, int64_t m, int64_t d, int dtype,
+                                int chunks, void* dbuf, size_t dbuf_bytes, lf_stream_t stream);
+
 /* Legacy forward with the reference's per-output tree reduction in the
    storage type, including its behaviour for d that is not a power of two.
    Replaces laplace::LaplaceSubtraction_reduce_forward_cuda

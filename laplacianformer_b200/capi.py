@@ -38,6 +38,9 @@ SIGNATURES = {
     "lf_laplace_sub_bwd": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I, _P]),
     "lf_laplace_sub_bwd_workspace_size": (ctypes.c_size_t, [_I64, _I64, _I64, _I64, _I]),
     "lf_laplace_sub_bwd_noalloc": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I, _P]),
+    "lf_laplace_sub_host_buffer_size": (ctypes.c_size_t, [_I64, _I64, _I64, _I64, _I, _I]),
+    "lf_laplace_sub_fwd_bwd_host": (_I, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I, _I, _P, ctypes.c_size_t,
+                                         _P]),
     "lf_laplace_sub_bwd_ws": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I, _P, ctypes.c_size_t, _P]),
     "lf_laplace_sub_reduce_fwd": (_I, [_P, _P, _P, _I64, _I64, _I64, _I64, _I, _P]),
     "lf_newton_inverse_supported": (_I, [_I64]),

@@ -268,23 +268,45 @@ def test_against_reference_module(cuda, ref_module, dtype):
     assert torch.all((dk.double() - dk_ref.double()).abs() <= tol * ga.sum(-2).unsqueeze(-2) + 1e-30)
 
 
-def test_host_pipeline_matches_device_calls(cuda):
+@pytest.mark.parametrize("shape,dtype,chunks", [
+    ((3, 2, 130, 32, 49), torch.float32, 4),   # balanced backward per chunk, ragged last chunk
+    ((7, 1, 70, 32, 49), torch.float16, 3),
+    ((2, 1, 40, 20, 196), torch.float32, 5),   # workspace-free backward (m > 64)
+    ((1, 2, 33, 17, 5), torch.bfloat16, 8),    # more chunks than slices
+], ids=str)
+def test_host_pipeline_matches_device_calls(cuda, shape, dtype, chunks):
     from laplacianformer_b200.streaming import HostPipeline
 
-    q, k, g = _inputs((3, 2, 130, 32, 49), torch.float32, seed=12)
+    B, H, N, D, M = shape
+    q, k, g = _inputs(shape, dtype, seed=12)
     hq, hk, hg = q.pin_memory(), k.pin_memory(), g.pin_memory()
-    hs = torch.empty(3, 2, 130, 49).pin_memory()
+    hs = torch.empty(B, H, N, M, dtype=dtype).pin_memory()
     hdq = torch.empty_like(q).pin_memory()
     hdk = torch.empty_like(k).pin_memory()
-    pipe = HostPipeline(q.shape, 49, device=cuda, chunks=4)
-    for _ in range(2):  # buffer reuse across calls
+    pipe = HostPipeline(q.shape, M, dtype=dtype, device=cuda, chunks=chunks)
+    s = capi.laplace_sub_fwd(q.to(cuda), k.to(cuda))
+    dq, dk = capi.laplace_sub_bwd(g.to(cuda), q.to(cuda), k.to(cuda))
+    torch.cuda.synchronize()
+    col = g.double().abs().sum(-2).unsqueeze(-2)
+    for _ in range(2):  # buffer and stream reuse across calls
+        hs.fill_(7.0), hdq.fill_(7.0), hdk.fill_(7.0)
         pipe(hq, hk, hg, hs, hdq, hdk)
         torch.cuda.synchronize()
-        s = capi.laplace_sub_fwd(q.to(cuda), k.to(cuda))
-        dq, dk = capi.laplace_sub_bwd(g.to(cuda), q.to(cuda), k.to(cuda))
-        torch.cuda.synchronize()
         assert torch.equal(hs, s.cpu())
-        assert torch.equal(hdq, dq.cpu()) and torch.equal(hdk, dk.cpu())
+        assert torch.equal(hdq, dq.cpu())
+        # dK^T partial sums are split per chunk: same value up to summation order
+        assert torch.all((hdk.double() - dk.cpu().double()).abs() <= _bwd_tol(dtype) * col)
+
+
+def test_host_pipeline_errors(cuda):
+    L = capi.lib()
+    need = L.lf_laplace_sub_host_buffer_size(4, 100, 49, 32, capi.LF_F32, 2)
+    assert need > 0
+    buf = torch.empty(need, dtype=torch.uint8, device=cuda)
+    h = torch.empty(4 * 100 * 49).pin_memory()
+    rc = L.lf_laplace_sub_fwd_bwd_host(h.data_ptr(), h.data_ptr(), h.data_ptr(), h.data_ptr(), h.data_ptr(),
+                                       h.data_ptr(), 4, 100, 49, 32, capi.LF_F32, 2, buf.data_ptr(), need - 1, None)
+    assert rc == capi.LF_ERR_INVALID and b"device buffer" in L.lf_last_error()
 
 
 def _bwd_plain(g, q, k):
