@@ -23,6 +23,15 @@ void LaplaceSubtraction_reduce_forward_cuda(const at::Tensor query, const at::Te
 void LaplaceSubtraction_backward_cuda(const at::Tensor gradOutput, const at::Tensor query,
                                       const at::Tensor key, at::Tensor gradQuery, at::Tensor gradKey);
 
+// output = exp(scale * LaplaceSub(query, key)) in one pass (S not stored).
+// No counterpart in the reference.
+void LaplaceKernel_forward_cuda(const at::Tensor query, const at::Tensor key, at::Tensor output, double scale);
+
+inline void LaplaceKernel_forward(const at::Tensor query, const at::Tensor key, at::Tensor output, double scale) {
+    if (query.is_cuda() && key.is_cuda()) return LaplaceKernel_forward_cuda(query, key, output, scale);
+    AT_ERROR("Not implemented on the CPU");
+}
+
 inline void LaplaceSubtraction_forward(const at::Tensor query, const at::Tensor key, at::Tensor output) {
     if (query.is_cuda() && key.is_cuda()) return LaplaceSubtraction_forward_cuda(query, key, output);
     AT_ERROR("Not implemented on the CPU");

@@ -98,6 +98,17 @@ LF_API int lf_laplace_sub_fwd(const void* q, const void* kT, void* s,
                        int64_t bh, int64_t n, int64_t m, int64_t d,
                        int dtype, lf_stream_t stream);
 
+/* Laplacian kernel matrix Kmat[b,i,j] = exp(scale * S[b,i,j]) with S as in
+   lf_laplace_sub_fwd (the same bit-exact channel sums), the exponential
+   applied in the accumulation type before the one rounding to the storage
+   type; the attention block uses scale = -1/sigma.  S is never written.
+   Gradients: dS = scale * Kmat * dKmat, then lf_laplace_sub_bwd.  No
+   counterpart in the reference (its attention applies exp as a separate
+   PyTorch op on the stored S). */
+LF_API int lf_laplace_kernel_fwd(const void* q, const void* kT, void* kmat,
+                          int64_t bh, int64_t n, int64_t m, int64_t d,
+                          int dtype, double scale, lf_stream_t stream);
+
 /* dQ[b,i,c] = sum_j G[b,i,j] * sign(Q[b,i,c] - KT[b,c,j]), sign(0) = 0.
    Replaces laplace::LaplaceSubtraction_backward_query_cuda
    (src/LaplaceSubtraction_cuda.cu:69-84 -> src/LaplaceSubtraction_cuda_kernel.cu:487-547). */

@@ -10,8 +10,9 @@ as follows (configuration 4 of the benchmark):
     out    = K_QL @ X @ (K_LK @ V)                     [B,H,N,D]
 
 Every L1 distance and the inverse run on the B200 kernels (through the
-autograd functions of :mod:`laplacianformer_b200.ops`); the exponentials and
-the small products are PyTorch ops.  The landmark kernel matrix and its
+autograd functions of :mod:`laplacianformer_b200.ops`), with each exponential
+fused into the distance kernel's store (S is never written); the small
+products are PyTorch ops.  The landmark kernel matrix and its
 inverse are kept in fp32 whatever the storage type of Q/K/V.
 """
 from __future__ import annotations
@@ -20,7 +21,7 @@ import math
 
 import torch
 
-from .ops import INIT_REFERENCE, PREC_SPLIT3, laplace_subtraction, newton_inverse
+from .ops import INIT_REFERENCE, PREC_SPLIT3, laplace_kernel, newton_inverse
 
 
 def pool_landmarks(k: torch.Tensor, grid: int, pool: int) -> torch.Tensor:
@@ -39,13 +40,12 @@ def laplacian_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, landm
     D = q.shape[-1]
     sigma = math.sqrt(D) if sigma is None else sigma
     L = landmarks
-    s_ql = laplace_subtraction(q, L.transpose(-1, -2).contiguous())          # [B,H,N,M]
-    s_lk = laplace_subtraction(L, k.transpose(-1, -2).contiguous())          # [B,H,M,N]
+    # exp(-S/sigma) is fused into the distance kernel: S is never stored
+    k_ql = laplace_kernel(q, L.transpose(-1, -2).contiguous(), -1.0 / sigma)          # [B,H,N,M]
+    k_lk = laplace_kernel(L, k.transpose(-1, -2).contiguous(), -1.0 / sigma)          # [B,H,M,N]
     Lf = L.float()
-    s_ll = laplace_subtraction(Lf, Lf.transpose(-1, -2).contiguous())        # [B,H,M,M] fp32
-    k_ql = torch.exp(-s_ql / sigma)
-    k_lk = torch.exp(-s_lk / sigma)
-    x = newton_inverse(torch.exp(-s_ll / sigma), iters, init_mode=init_mode, precision=precision)
+    k_ll = laplace_kernel(Lf, Lf.transpose(-1, -2).contiguous(), -1.0 / sigma)       # [B,H,M,M] fp32
+    x = newton_inverse(k_ll, iters, init_mode=init_mode, precision=precision)
     kv = k_lk @ v                                                            # [B,H,M,D]
     return k_ql @ (x.to(q.dtype) @ kv)
 

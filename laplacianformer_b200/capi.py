@@ -33,6 +33,7 @@ SIGNATURES = {
     "lf_cudart_version": (_I, []),
     "lf_version": (_I, []),
     "lf_laplace_sub_fwd": (_I, [_P, _P, _P, _I64, _I64, _I64, _I64, _I, _P]),
+    "lf_laplace_kernel_fwd": (_I, [_P, _P, _P, _I64, _I64, _I64, _I64, _I, _D, _P]),
     "lf_laplace_sub_bwd_query": (_I, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I, _P]),
     "lf_laplace_sub_bwd_key": (_I, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I, _P]),
     "lf_laplace_sub_bwd": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I, _P]),
@@ -119,6 +120,17 @@ def laplace_sub_fwd(q, kT, out=None):
         out = torch.empty(q.shape[0], q.shape[1], n, m, device=q.device, dtype=q.dtype)
     _check(lib().lf_laplace_sub_fwd(_ptr(q), _ptr(kT), _ptr(out), bh, n, m, d, dtype_code(q), _stream(q)),
            "lf_laplace_sub_fwd")
+    return out
+
+
+def laplace_kernel_fwd(q, kT, scale, out=None):
+    """Kmat = exp(scale * LaplaceSub(q, kT)) in one launch (S is not stored)."""
+    _need_cuda(q, kT, out)
+    bh, n, m, d = _dims(q, kT)
+    if out is None:
+        out = torch.empty(q.shape[0], q.shape[1], n, m, device=q.device, dtype=q.dtype)
+    _check(lib().lf_laplace_kernel_fwd(_ptr(q), _ptr(kT), _ptr(out), bh, n, m, d, dtype_code(q), float(scale),
+                                       _stream(q)), "lf_laplace_kernel_fwd")
     return out
 
 

@@ -127,6 +127,16 @@ __device__ __forceinline__ void accum_chunk(A (&acc)[TM][MC], const A (&qr)[TM][
     }
 }
 
+// Forward epilogue: S itself, or exp(escale * S) for the Laplacian kernel
+// matrix (the attention block's exp(-S/sigma)); the exponential is CUDA's
+// expf / exp on the accumulation type.
+template <typename A>
+__device__ __forceinline__ A fwd_epilogue(A acc, A escale, bool do_exp) {
+    if (!do_exp) return acc;
+    if constexpr (sizeof(A) == 4) return expf(escale * acc);
+    else return exp(escale * acc);
+}
+
 // One CTA = kThreads*TM query rows of one (b,h); thread t owns rows
 // base + t + kThreads*r and keeps DR channels of each in registers.  When
 // d <= DR the rows are loaded once and zero padded to DR (padded channels add
@@ -136,7 +146,8 @@ __device__ __forceinline__ void accum_chunk(A (&acc)[TM][MC], const A (&qr)[TM][
 template <typename T, int TM, int MC, int DR>
 __global__ void __launch_bounds__(kThreads)
 lsub_fwd_kernel(const T* __restrict__ q, const T* __restrict__ kT, T* __restrict__ s,
-                int n, int m, int d, int tiles_per_bh, bool vec, bool stage_out) {
+                int n, int m, int d, int tiles_per_bh, bool vec, bool stage_out,
+                typename Elem<T>::acc escale, bool do_exp) {
     using A = typename Elem<T>::acc;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     A* ks = reinterpret_cast<A*>(smem_raw);
@@ -220,7 +231,7 @@ lsub_fwd_kernel(const T* __restrict__ q, const T* __restrict__ kT, T* __restrict
                 T* out = so + (threadIdx.x + kThreads * r) * m + mc;
 #pragma unroll
                 for (int j = 0; j < MC; ++j)
-                    if (mc + j < m) out[j] = Elem<T>::store(acc[r][j]);
+                    if (mc + j < m) out[j] = Elem<T>::store(fwd_epilogue(acc[r][j], escale, do_exp));
                 continue;
             }
             int64_t row = row0 + (int64_t)kThreads * r;
@@ -228,7 +239,7 @@ lsub_fwd_kernel(const T* __restrict__ q, const T* __restrict__ kT, T* __restrict
             T* out = Sb + row * m + mc;
 #pragma unroll
             for (int j = 0; j < MC; ++j)
-                if (mc + j < m) out[j] = Elem<T>::store(acc[r][j]);
+                if (mc + j < m) out[j] = Elem<T>::store(fwd_epilogue(acc[r][j], escale, do_exp));
         }
     }
     if (!stage_out) return;
@@ -288,7 +299,7 @@ size_t fwd_smem_total(int64_t m, int64_t d) {
 
 template <typename T, int TM, int MC, int DR>
 int launch_fwd_mc(const T* q, const T* kT, T* s, int64_t bh, int64_t n, int64_t m, int64_t d,
-                  cudaStream_t st) {
+                  cudaStream_t st, double escale, bool do_exp) {
     size_t smem = fwd_smem_total<T, TM, MC, DR>(m, d);
     const bool stage = fwd_stage_bytes<T, TM>(m) != 0 && smem <= (size_t)max_optin_smem();
     if (!stage) smem = fwd_smem<T, TM, MC, DR>(m, d);
@@ -304,7 +315,8 @@ int launch_fwd_mc(const T* q, const T* kT, T* s, int64_t bh, int64_t n, int64_t 
     int64_t blocks = bh * tiles;
     if (blocks > 0x7fffffff) { set_error("too many blocks"); return LF_ERR_UNSUPPORTED; }
     bool vec = (d % 16 == 0) && aligned(q, 16);
-    kern<<<(unsigned)blocks, kThreads, smem, st>>>(q, kT, s, (int)n, (int)m, (int)d, tiles, vec, stage);
+    kern<<<(unsigned)blocks, kThreads, smem, st>>>(q, kT, s, (int)n, (int)m, (int)d, tiles, vec, stage,
+                                                   (typename Elem<T>::acc)escale, do_exp);
     return check_launch("lsub_fwd_kernel");
 }
 
@@ -312,7 +324,8 @@ int launch_fwd_mc(const T* q, const T* kT, T* s, int64_t bh, int64_t n, int64_t 
 // per thread halves the CTA's rows.  Take one row only when that fills the
 // last wave of CTAs clearly better.
 template <typename T, int MC, int DR>
-int launch_fwd_tm(const T* Q, const T* K, T* S, int64_t bh, int64_t n, int64_t m, int64_t d, cudaStream_t st) {
+int launch_fwd_tm(const T* Q, const T* K, T* S, int64_t bh, int64_t n, int64_t m, int64_t d, cudaStream_t st,
+                 double escale, bool do_exp) {
     if constexpr (DR <= 32) {
         const size_t smem1 = fwd_smem_total<T, 1, MC, DR>(m, d);
         const size_t smem2 = fwd_smem_total<T, 2, MC, DR>(m, d);
@@ -323,22 +336,23 @@ int launch_fwd_tm(const T* Q, const T* K, T* S, int64_t bh, int64_t n, int64_t m
             if (smem2 > 48 * 1024) cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem2);
             double e1 = wave_efficiency(bh * ((n + kThreads - 1) / kThreads), cta_slots(k1, smem1));
             double e2 = wave_efficiency(bh * ((n + 2 * kThreads - 1) / (2 * kThreads)), cta_slots(k2, smem2));
-            if (e1 > e2 + 0.05) return launch_fwd_mc<T, 1, MC, DR>(Q, K, S, bh, n, m, d, st);
+            if (e1 > e2 + 0.05) return launch_fwd_mc<T, 1, MC, DR>(Q, K, S, bh, n, m, d, st, escale, do_exp);
         }
-        return launch_fwd_mc<T, 2, MC, DR>(Q, K, S, bh, n, m, d, st);
+        return launch_fwd_mc<T, 2, MC, DR>(Q, K, S, bh, n, m, d, st, escale, do_exp);
     } else {
-        return launch_fwd_mc<T, 1, MC, DR>(Q, K, S, bh, n, m, d, st);
+        return launch_fwd_mc<T, 1, MC, DR>(Q, K, S, bh, n, m, d, st, escale, do_exp);
     }
 }
 
 template <typename T, int DR>
-int launch_fwd_dr(const T* Q, const T* K, T* S, int64_t bh, int64_t n, int64_t m, int64_t d, cudaStream_t st) {
+int launch_fwd_dr(const T* Q, const T* K, T* S, int64_t bh, int64_t n, int64_t m, int64_t d, cudaStream_t st,
+                 double escale, bool do_exp) {
     switch (pick_mc(m)) {
-        case 4: return launch_fwd_tm<T, 4, DR>(Q, K, S, bh, n, m, d, st);
-        case 5: return launch_fwd_tm<T, 5, DR>(Q, K, S, bh, n, m, d, st);
-        case 6: return launch_fwd_tm<T, 6, DR>(Q, K, S, bh, n, m, d, st);
-        case 7: return launch_fwd_tm<T, 7, DR>(Q, K, S, bh, n, m, d, st);
-        default: return launch_fwd_tm<T, 8, DR>(Q, K, S, bh, n, m, d, st);
+        case 4: return launch_fwd_tm<T, 4, DR>(Q, K, S, bh, n, m, d, st, escale, do_exp);
+        case 5: return launch_fwd_tm<T, 5, DR>(Q, K, S, bh, n, m, d, st, escale, do_exp);
+        case 6: return launch_fwd_tm<T, 6, DR>(Q, K, S, bh, n, m, d, st, escale, do_exp);
+        case 7: return launch_fwd_tm<T, 7, DR>(Q, K, S, bh, n, m, d, st, escale, do_exp);
+        default: return launch_fwd_tm<T, 8, DR>(Q, K, S, bh, n, m, d, st, escale, do_exp);
     }
 }
 
@@ -346,19 +360,19 @@ int launch_fwd_dr(const T* Q, const T* K, T* S, int64_t bh, int64_t n, int64_t m
 // or 64 channels x 1 row), 32-channel chunks beyond; fp64 uses 16 channels.
 template <typename T>
 int launch_fwd(const void* q, const void* kT, void* s, int64_t bh, int64_t n, int64_t m, int64_t d,
-               cudaStream_t st) {
+               cudaStream_t st, double escale = 0.0, bool do_exp = false) {
     const T* Q = static_cast<const T*>(q);
     const T* K = static_cast<const T*>(kT);
     T* S = static_cast<T*>(s);
     if constexpr (sizeof(T) == 8) {
-        return launch_fwd_dr<T, 16>(Q, K, S, bh, n, m, d, st);
+        return launch_fwd_dr<T, 16>(Q, K, S, bh, n, m, d, st, escale, do_exp);
     } else {
-        if (d <= 16) return launch_fwd_dr<T, 16>(Q, K, S, bh, n, m, d, st);
+        if (d <= 16) return launch_fwd_dr<T, 16>(Q, K, S, bh, n, m, d, st, escale, do_exp);
         if (d <= 32) {
-            return launch_fwd_dr<T, 32>(Q, K, S, bh, n, m, d, st);
+            return launch_fwd_dr<T, 32>(Q, K, S, bh, n, m, d, st, escale, do_exp);
         }
-        if (d <= 64) return launch_fwd_dr<T, 64>(Q, K, S, bh, n, m, d, st);
-        return launch_fwd_dr<T, 32>(Q, K, S, bh, n, m, d, st);
+        if (d <= 64) return launch_fwd_dr<T, 64>(Q, K, S, bh, n, m, d, st, escale, do_exp);
+        return launch_fwd_dr<T, 32>(Q, K, S, bh, n, m, d, st, escale, do_exp);
     }
 }
 
@@ -1473,6 +1487,37 @@ extern "C" int lf_laplace_sub_fwd(const void* q, const void* kT, void* s, int64_
         return LF_OK;
     }
     LF_DISPATCH(dtype, T, return launch_fwd<T>(q, kT, s, bh, n, m, d, st));
+    return LF_OK;
+}
+
+template <typename T>
+__global__ void fill_one_kernel(T* p, int64_t count) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < count; i += (int64_t)gridDim.x * blockDim.x)
+        p[i] = Elem<T>::store(typename Elem<T>::acc(1));
+}
+
+extern "C" int lf_laplace_kernel_fwd(const void* q, const void* kT, void* kmat, int64_t bh, int64_t n, int64_t m,
+                                     int64_t d, int dtype, double scale, lf_stream_t stream) {
+    clear_error();
+    int rc = check_args(q, kT, kmat, bh, n, m, d, dtype);
+    if (rc) return rc;
+    if (!(scale == scale) || scale > 3.0e38 || scale < -3.0e38) {
+        set_error("lf_laplace_kernel_fwd: scale must be finite");
+        return LF_ERR_INVALID;
+    }
+    if (bh == 0 || n == 0 || m == 0) return LF_OK;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (d == 0) {  // S = 0, exp(0) = 1
+        const int64_t count = bh * n * m;
+        int64_t blocks = (count + kThreads - 1) / kThreads;
+        if (blocks > (int64_t)num_sms() * 8) blocks = (int64_t)num_sms() * 8;
+        LF_DISPATCH(dtype, T, {
+            fill_one_kernel<T><<<(unsigned)blocks, kThreads, 0, st>>>(static_cast<T*>(kmat), count);
+            return check_launch("fill_one_kernel");
+        });
+        return LF_OK;
+    }
+    LF_DISPATCH(dtype, T, return launch_fwd<T>(q, kT, kmat, bh, n, m, d, st, scale, true));
     return LF_OK;
 }
 

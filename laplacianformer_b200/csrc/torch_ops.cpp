@@ -85,6 +85,16 @@ void LaplaceSubtraction_forward_cuda(const at::Tensor query, const at::Tensor ke
              "LaplaceSubtraction_forward");
 }
 
+void LaplaceKernel_forward_cuda(const at::Tensor query, const at::Tensor key, at::Tensor output, double scale) {
+    shape_check(query, key);
+    out_check(output, query, {query.size(0), query.size(1), query.size(2), key.size(3)}, "output");
+    c10::cuda::CUDAGuard guard(query.device());
+    Dims s = dims_of(query, key);
+    raise_on(lf_laplace_kernel_fwd(query.data_ptr(), key.data_ptr(), output.data_ptr(), s.bh, s.n, s.m, s.d,
+                                   dtype_code(query), scale, stream_of(query)),
+             "LaplaceKernel_forward");
+}
+
 void LaplaceSubtraction_backward_query_cuda(const at::Tensor gradOutput, const at::Tensor query,
                                             const at::Tensor key, at::Tensor gradQuery) {
     shape_check(query, key);

@@ -60,6 +60,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           "LaplaceSubtraction_backward (gradOutput, query, key, gradQuery, gradKey): both gradients in one pass; "
           "pass an undefined tensor (None) to skip one",
           py::arg("gradOutput"), py::arg("query"), py::arg("key"), py::arg("gradQuery"), py::arg("gradKey"));
+    m.def("LaplaceKernel_forward", &LaplaceKernel_forward,
+          "LaplaceKernel_forward (query, key, output, scale): output = exp(scale * LaplaceSub(query, key)), fused",
+          py::arg("query"), py::arg("key"), py::arg("output"), py::arg("scale"));
     m.def("NewtonInverse_forward_ex", &NewtonInverse_forward_ex,
           "NewtonInverse_forward_ex (mat, output, iter, init_mode, reg, precision)", py::arg("mat"), py::arg("output"),
           py::arg("iter"), py::arg("init_mode") = 0, py::arg("reg") = 0.01, py::arg("precision") = 0);

@@ -65,6 +65,37 @@ def laplace_subtraction(query: torch.Tensor, key: torch.Tensor) -> torch.Tensor:
     return LaplaceSubtractionFn.apply(query, key)
 
 
+class LaplaceKernelFn(torch.autograd.Function):
+    """Kmat = exp(scale * LaplaceSub(Q, K^T)), forward fused into one kernel;
+    backward dS = scale * Kmat * dKmat, then the fused LaplaceSub backward."""
+
+    @staticmethod
+    def forward(ctx, query, key, scale):
+        query = query.contiguous()
+        key = key.contiguous()
+        out = query.new_empty(query.shape[0], query.shape[1], query.shape[2], key.shape[3])
+        ext().LaplaceKernel_forward(query, key, out, float(scale))
+        ctx.save_for_backward(query, key, out)
+        ctx.scale = float(scale)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad):
+        query, key, out = ctx.saved_tensors
+        need_q, need_k = ctx.needs_input_grad[0], ctx.needs_input_grad[1]
+        dq = torch.empty_like(query) if need_q else None
+        dk = torch.empty_like(key) if need_k else None
+        if need_q or need_k:
+            gs = (grad * out) * ctx.scale
+            ext().LaplaceSubtraction_backward(gs.contiguous(), query, key, dq, dk)
+        return dq, dk, None
+
+
+def laplace_kernel(query: torch.Tensor, key: torch.Tensor, scale: float) -> torch.Tensor:
+    """exp(scale * sum_d |query - key|) with key given as [B,H,D,M]; S is never materialised."""
+    return LaplaceKernelFn.apply(query, key, scale)
+
+
 class NewtonInverseFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, mat, iters, init_mode, reg, precision):

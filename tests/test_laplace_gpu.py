@@ -361,3 +361,39 @@ def test_balanced_backward_workspace_errors(cuda):
     q2, k2, g2 = (t.to(cuda) for t in _inputs((1, 1, 9, 100, 256), torch.float32))
     assert capi.laplace_sub_bwd_workspace_size(q2, k2) == 0
     assert capi.laplace_sub_bwd_workspace_size(q.double(), k.double()) == 0
+
+
+@pytest.mark.parametrize("shape", [(2, 2, 70, 32, 49), (1, 3, 33, 17, 5), (2, 1, 50, 64, 256), (1, 1, 9, 100, 20),
+                                   (1, 1, 4, 0, 3)], ids=str)
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float64, torch.float16, torch.bfloat16], ids=str)
+def test_laplace_kernel_fused_exp(cuda, shape, dtype):
+    """exp(scale*S) in the forward's store equals exp of the (bit-exact) S."""
+    q, k, _ = _inputs(shape, dtype, seed=21)
+    scale = -1.0 / 5.0
+    got = capi.laplace_kernel_fwd(q.to(cuda), k.to(cuda), scale)
+    torch.cuda.synchronize()
+    if shape[3] == 0:
+        assert torch.all(got.float() == 1.0)
+        return
+    wide = dtype in (torch.float16, torch.bfloat16)  # 16-bit inputs accumulate in fp32
+    ref_s = np.asarray(O.laplace_fwd(q.float() if wide else q, k.float() if wide else k), dtype=np.float64)
+    ref = np.exp(scale * ref_s)
+    # expf of the fp32-rounded argument: a few ulp in fp32; one rounding to 16-bit types
+    rtol = {torch.float32: 4e-6, torch.float64: 1e-14, torch.float16: 1e-3, torch.bfloat16: 8e-3}[dtype]
+    np.testing.assert_allclose(_np(got).astype(np.float64), ref, rtol=rtol, atol=0)
+
+
+def test_laplace_kernel_autograd_matches_composition(cuda):
+    from laplacianformer_b200.ops import laplace_kernel, laplace_subtraction
+
+    q, k, _ = _inputs((2, 2, 70, 32, 49), torch.float32, seed=22)
+    q1, k1 = q.to(cuda).requires_grad_(), k.to(cuda).requires_grad_()
+    q2, k2 = q.to(cuda).requires_grad_(), k.to(cuda).requires_grad_()
+    g = torch.randn(2, 2, 70, 49, device=cuda)
+    a = laplace_kernel(q1, k1, -0.2)
+    b = torch.exp(-0.2 * laplace_subtraction(q2, k2))
+    torch.testing.assert_close(a, b, rtol=4e-6, atol=0)
+    (a * g).sum().backward()
+    (b * g).sum().backward()
+    torch.testing.assert_close(q1.grad, q2.grad, rtol=1e-4, atol=1e-5)
+    torch.testing.assert_close(k1.grad, k2.grad, rtol=1e-4, atol=1e-4)
