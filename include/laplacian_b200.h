@@ -229,6 +229,17 @@ LF_API int lf_newton_inverse_fwd_ex(const void* a, void* x, int64_t batch, int64
                              int dtype, int init_mode, double reg, int precision,
                              lf_stream_t stream);
 
+/* Newton–Schulz inverse of the landmark kernel matrix built in the same
+   kernel: A_b = exp(scale * S_b), S_b[i][j] = sum_k |L_b[i][k] - L_b[j][k]|
+   (bit-identical to lf_laplace_kernel_fwd(L, L^T, scale)), then
+   lf_newton_inverse_fwd_ex(A, ...) on the tensor cores — A never goes to
+   global memory.  L is fp32 [batch, n, d], X fp32 [batch, n, n]; n <= 128,
+   d <= 128, precision LF_NS_PREC_SPLIT3 or LF_NS_PREC_MIXED.  No counterpart
+   in the reference, where A is three separate PyTorch/CUDA steps. */
+LF_API int lf_laplace_newton_inverse_fwd(const void* lmk, void* x, int64_t batch, int64_t n, int64_t d,
+                                  double scale, int iters, int init_mode, double reg, int precision,
+                                  lf_stream_t stream);
+
 /* dA = -(V^T G V^T) for the inverse V and upstream gradient G.
    Replaces laplace::NewtonInverse_backward_cuda (src/NewtonInverse_cuda_kernel.cu:796-833). */
 LF_API int lf_newton_inverse_bwd(const void* g, const void* v, void* da,

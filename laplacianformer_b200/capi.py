@@ -47,6 +47,7 @@ SIGNATURES = {
     "lf_newton_inverse_supported": (_I, [_I64]),
     "lf_newton_inverse_fwd": (_I, [_P, _P, _I64, _I64, _I, _I, _P]),
     "lf_newton_inverse_fwd_ex": (_I, [_P, _P, _I64, _I64, _I, _I, _I, _D, _I, _P]),
+    "lf_laplace_newton_inverse_fwd": (_I, [_P, _P, _I64, _I64, _I64, _D, _I, _I, _D, _I, _P]),
     "lf_newton_inverse_bwd": (_I, [_P, _P, _P, _I64, _I64, _I, _P]),
     "lf_newton_inverse_residual": (_I, [_P, _P, _P, _I64, _I64, _D, _I, _P]),
     "lf_device_status": (_I, [_I]),
@@ -205,6 +206,23 @@ def newton_inverse_fwd(a, iters, init_mode=INIT_REFERENCE, reg=None, precision=P
         reg = 0.01 if init_mode == INIT_REFERENCE else 0.0
     _check(lib().lf_newton_inverse_fwd_ex(_ptr(a), _ptr(out), batch, n, int(iters), dtype_code(a), int(init_mode),
                                           float(reg), int(precision), _stream(a)), "lf_newton_inverse_fwd_ex")
+    return out
+
+
+def laplace_newton_inverse_fwd(lmk, scale, iters, init_mode=INIT_REFERENCE, reg=None, precision=PREC_SPLIT3,
+                                out=None):
+    """X = NewtonInverse(exp(scale * LaplaceSub(L, L^T))) in one kernel; lmk fp32 [..., n, d]."""
+    _need_cuda(lmk, out)
+    if lmk.dtype != torch.float32 or not lmk.is_contiguous():
+        raise ValueError("landmarks must be contiguous fp32")
+    n, d = lmk.shape[-2], lmk.shape[-1]
+    batch = lmk.numel() // (n * d) if n * d else 0
+    out = torch.empty(*lmk.shape[:-1], n, device=lmk.device, dtype=torch.float32) if out is None else out
+    if reg is None:
+        reg = 0.01 if init_mode == INIT_REFERENCE else 0.0
+    _check(lib().lf_laplace_newton_inverse_fwd(_ptr(lmk), _ptr(out), batch, n, d, float(scale), int(iters),
+                                               int(init_mode), float(reg), int(precision), _stream(lmk)),
+           "lf_laplace_newton_inverse_fwd")
     return out
 
 

@@ -337,7 +337,7 @@ __device__ __forceinline__ int stage_idx(int i, int c) { return i * kTile + (c ^
 template <typename T>
 __global__ void __launch_bounds__(kNsThreads, 1)
 ns_tc_fwd_kernel(const T* __restrict__ a, T* __restrict__ x, int n, int iters, int mode, float reg,
-                 int precision) {
+                 int precision, const float* __restrict__ lmk, int ld, float lscale) {
     extern __shared__ __align__(16) unsigned char smem_raw[];  // re-aligned to 1024 below
     unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     unsigned char* Ph = base;
@@ -365,17 +365,48 @@ ns_tc_fwd_kernel(const T* __restrict__ a, T* __restrict__ x, int n, int iters, i
     if (warp == 0) tmem_alloc(&sh.tmem_base, kTmemCols);
     __syncthreads();
 
+    // ---- optional: A from landmarks -------------------------------------------
+    // With lmk != nullptr, A[i][c] = exp(lscale * sum_k |L[i][k] - L[c][k]|)
+    // is formed here (the channel sum in order with the LaplaceSub forward's
+    // fp32 operations, so A is bit-identical to lf_laplace_kernel_fwd(L, L^T)).
+    // L^T of this matrix is staged as LT[k][c] in the Vh/Vl region (free until
+    // V0 is written after the set-up): row i is a warp-uniform broadcast and a
+    // lane's four columns one 16-byte load.
+    float* LT = reinterpret_cast<float*>(Vh);
+    if (lmk) {
+        const float* Lb = lmk + mat * (int64_t)n * ld;
+        for (int e = tid; e < ld * kTile; e += kNsThreads) {
+            const int c = e / ld, k = e - c * ld;  // coalesced read of L[c][k]
+            LT[k * kTile + c] = (c < n) ? Lb[(int64_t)c * ld + k] : 0.f;
+        }
+        __syncthreads();
+    }
+
     // ---- set-up: P = A + reg I into the staging tile -------------------------
     // Warp w loads rows w, w+16, ...; lane l holds columns 4l..4l+3.
     float mx[4] = {-1e30f, 0.f, 0.f, 0.f};  // signed row sum, |row| sum, max|P|, |col| sum
     float colacc[4] = {0.f, 0.f, 0.f, 0.f};
     for (int i = warp; i < kTile; i += kNsThreads / 32) {
         float v[4];
+        float lsum[4] = {0.f, 0.f, 0.f, 0.f};
+        if (lmk && i < n) {
+            for (int k = 0; k < ld; ++k) {
+                const float li = LT[k * kTile + i];
+                const float4 lc = *reinterpret_cast<const float4*>(LT + k * kTile + 4 * lane);
+                lsum[0] = add_abs_ftz(lsum[0], sub_ftz(li, lc.x));
+                lsum[1] = add_abs_ftz(lsum[1], sub_ftz(li, lc.y));
+                lsum[2] = add_abs_ftz(lsum[2], sub_ftz(li, lc.z));
+                lsum[3] = add_abs_ftz(lsum[3], sub_ftz(li, lc.w));
+            }
+        }
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
             int c = 4 * lane + e;
             float t = 0.f;
-            if (i < n && c < n) t = Elem<T>::load(A[(int64_t)i * n + c]) + (i == c ? reg : 0.f);
+            if (i < n && c < n) {
+                const float av = lmk ? expf(lscale * lsum[e]) : Elem<T>::load(A[(int64_t)i * n + c]);
+                t = av + (i == c ? reg : 0.f);
+            }
             v[e] = t;
             stage[stage_idx(i, c)] = t;
             colacc[e] += fabsf(t);
@@ -393,10 +424,17 @@ ns_tc_fwd_kernel(const T* __restrict__ a, T* __restrict__ x, int n, int iters, i
             mx[1] = fmaxf(mx[1], ra);
         }
     }
+    // column |sums|: per-warp partials combined in warp order (deterministic,
+    // so equal inputs give equal bits); Ph is free until P is split below
+    float* cpart = reinterpret_cast<float*>(Ph);  // [16 warps][kTile]
 #pragma unroll
-    for (int e = 0; e < 4; ++e) atomicAdd(&sh.colsum[4 * lane + e], colacc[e]);
+    for (int e = 0; e < 4; ++e) cpart[warp * kTile + 4 * lane + e] = colacc[e];
     __syncthreads();
-    if (tid < kTile) mx[3] = sh.colsum[tid];
+    if (tid < kTile) {
+        float cs = 0.f;
+        for (int w = 0; w < kNsThreads / 32; ++w) cs += cpart[w * kTile + tid];
+        mx[3] = cs;
+    }
     block_max4(mx, sh);
     const float pmax = mx[2];
     const float v0_scale = (mode == LF_NS_INIT_REFERENCE) ? __fdiv_rn(1.8f, mx[0] * mx[0])
@@ -1011,9 +1049,52 @@ int launch_tc_fwd(const void* a, void* x, int64_t batch, int64_t n, int iters, i
     auto kern = ns_tc_fwd_kernel<T>;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     kern<<<(unsigned)batch, kNsThreads, smem, st>>>(static_cast<const T*>(a), static_cast<T*>(x), (int)n, iters,
-                                                    mode, reg, precision);
+                                                    mode, reg, precision, nullptr, 0, 0.f);
     return check_launch("ns_tc_fwd_kernel");
 }
+
+}  // namespace
+}  // namespace lfb
+
+extern "C" int lf_laplace_newton_inverse_fwd(const void* lmk, void* x, int64_t batch, int64_t n, int64_t d,
+                                             double scale, int iters, int init_mode, double reg, int precision,
+                                             lf_stream_t stream) {
+    using namespace lfb;
+    clear_error();
+    if (batch < 0 || n < 0 || d < 0) { set_error("negative size"); return LF_ERR_INVALID; }
+    if (batch == 0 || n == 0) return LF_OK;
+    if (!lmk || !x) { set_error("null pointer"); return LF_ERR_INVALID; }
+    if (n > kTile || d < 1 || d * kTile * 4 > 2 * kOpBytes) {
+        set_error("lf_laplace_newton_inverse_fwd supports n <= %d and 1 <= d <= %d (got n=%lld, d=%lld)", kTile,
+                  2 * kOpBytes / (kTile * 4), (long long)n, (long long)d);
+        return LF_ERR_UNSUPPORTED;
+    }
+    if (init_mode != LF_NS_INIT_REFERENCE && init_mode != LF_NS_INIT_SCALED_TRANSPOSE) {
+        set_error("unknown init mode %d", init_mode);
+        return LF_ERR_INVALID;
+    }
+    if (precision != LF_NS_PREC_SPLIT3 && precision != LF_NS_PREC_MIXED) {
+        set_error("lf_laplace_newton_inverse_fwd runs on the tensor cores: precision must be split3 or mixed");
+        return LF_ERR_INVALID;
+    }
+    if (batch > 0x7fffffff) { set_error("batch too large"); return LF_ERR_UNSUPPORTED; }
+    if (iters < 0) iters = 0;
+    const size_t smem = tc_smem_bytes();
+    if (smem > (size_t)max_optin_smem()) {
+        set_error("NewtonInverse tensor-core path needs %zu bytes of shared memory", smem);
+        return LF_ERR_UNSUPPORTED;
+    }
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    auto kern = ns_tc_fwd_kernel<float>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    kern<<<(unsigned)batch, kNsThreads, smem, st>>>(nullptr, static_cast<float*>(x), (int)n, iters, init_mode,
+                                                    (float)reg, precision, static_cast<const float*>(lmk), (int)d,
+                                                    (float)scale);
+    return check_launch("ns_tc_fwd_kernel");
+}
+
+namespace lfb {
+namespace {
 
 template <typename T>
 int launch_simt_fwd(const void* a, void* x, int64_t batch, int64_t n, int iters, int mode, double reg,

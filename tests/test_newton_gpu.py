@@ -210,3 +210,28 @@ def test_bounded_wait_reports_timeout(cuda):
     X = capi.newton_inverse_fwd(A, 10)
     torch.cuda.synchronize()
     assert torch.isfinite(X).all()
+
+
+@pytest.mark.parametrize("n,d", [(49, 64), (128, 64), (17, 5), (100, 128)], ids=str)
+@pytest.mark.parametrize("init_mode", [capi.INIT_REFERENCE, capi.INIT_SCALED_TRANSPOSE], ids=str)
+def test_landmark_inverse_fused_equals_two_step(cuda, n, d, init_mode):
+    """A = exp(scale*S_LL) built inside the inverse kernel gives the same bits
+    as lf_laplace_kernel_fwd followed by the inverse of that stored A."""
+    g = torch.Generator().manual_seed(n * 1000 + d)
+    L = torch.randn(3, 2, n, d, generator=g).to(cuda)
+    scale = -1.0 / (d ** 0.5)
+    A = capi.laplace_kernel_fwd(L, L.transpose(-1, -2).contiguous(), scale)
+    for prec in (capi.PREC_SPLIT3, capi.PREC_MIXED):
+        x2 = capi.newton_inverse_fwd(A, 10, init_mode=init_mode, precision=prec)
+        x1 = capi.laplace_newton_inverse_fwd(L, scale, 10, init_mode=init_mode, precision=prec)
+        torch.cuda.synchronize()
+        assert torch.equal(x1, x2)
+
+
+def test_landmark_inverse_fused_rejects_unsupported(cuda):
+    L = torch.randn(1, 129, 8, device=cuda)
+    with pytest.raises(RuntimeError, match="n <= 128"):
+        capi.laplace_newton_inverse_fwd(L, -0.1, 5)
+    L = torch.randn(1, 16, 8, device=cuda)
+    with pytest.raises(RuntimeError, match="precision"):
+        capi.laplace_newton_inverse_fwd(L, -0.1, 5, precision=capi.PREC_FP32_SIMT)
