@@ -21,7 +21,7 @@ import math
 
 import torch
 
-from .ops import INIT_REFERENCE, PREC_SPLIT3, laplace_kernel, newton_inverse
+from .ops import INIT_REFERENCE, PREC_SPLIT3, landmark_inverse, laplace_kernel, newton_inverse
 
 
 def pool_landmarks(k: torch.Tensor, grid: int, pool: int) -> torch.Tensor:
@@ -43,9 +43,14 @@ def laplacian_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, landm
     # exp(-S/sigma) is fused into the distance kernel: S is never stored
     k_ql = laplace_kernel(q, L.transpose(-1, -2).contiguous(), -1.0 / sigma)          # [B,H,N,M]
     k_lk = laplace_kernel(L, k.transpose(-1, -2).contiguous(), -1.0 / sigma)          # [B,H,M,N]
-    Lf = L.float()
-    k_ll = laplace_kernel(Lf, Lf.transpose(-1, -2).contiguous(), -1.0 / sigma)       # [B,H,M,M] fp32
-    x = newton_inverse(k_ll, iters, init_mode=init_mode, precision=precision)
+    Lf = L.float().contiguous()
+    M, D = Lf.shape[-2], Lf.shape[-1]
+    if M <= 128 and D <= 128 and precision in (0, 1):
+        # landmark kernel matrix built inside the inverse kernel
+        x = landmark_inverse(Lf, -1.0 / sigma, iters, init_mode=init_mode, precision=precision)
+    else:
+        k_ll = laplace_kernel(Lf, Lf.transpose(-1, -2).contiguous(), -1.0 / sigma)   # [B,H,M,M] fp32
+        x = newton_inverse(k_ll, iters, init_mode=init_mode, precision=precision)
     kv = k_lk @ v                                                            # [B,H,M,D]
     return k_ql @ (x.to(q.dtype) @ kv)
 

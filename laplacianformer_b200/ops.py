@@ -121,6 +121,47 @@ def newton_inverse(mat: torch.Tensor, iters: int, init_mode: int = INIT_REFERENC
     return NewtonInverseFn.apply(mat, iters, init_mode, reg, precision)
 
 
+class LandmarkInverseFn(torch.autograd.Function):
+    """X = NewtonInverse(exp(scale * LaplaceSub(L, L^T))) with A built inside
+    the inverse kernel (lf_laplace_newton_inverse_fwd).  Backward:
+    dA = -X^T G X^T (the inverse's analytic backward), dS = scale * A * dA with
+    A recomputed by the fused exp forward, then the LaplaceSub backward with L
+    as both query and key: dL = dQ + (dK^T)^T."""
+
+    @staticmethod
+    def forward(ctx, lmk, scale, iters, init_mode, reg, precision):
+        from . import capi
+
+        lmk = lmk.contiguous()
+        x = capi.laplace_newton_inverse_fwd(lmk, scale, iters, init_mode=init_mode, reg=reg, precision=precision)
+        ctx.save_for_backward(lmk, x)
+        ctx.scale = float(scale)
+        return x
+
+    @staticmethod
+    def backward(ctx, grad):
+        lmk, x = ctx.saved_tensors
+        da = torch.empty_like(x)
+        ext().NewtonInverse_backward(grad.contiguous(), x, da)
+        lT = lmk.transpose(-1, -2).contiguous()
+        a = torch.empty_like(x)
+        ext().LaplaceKernel_forward(lmk, lT, a, ctx.scale)
+        ds = (da * a) * ctx.scale
+        dq = torch.empty_like(lmk)
+        dkT = torch.empty_like(lT)
+        ext().LaplaceSubtraction_backward(ds.contiguous(), lmk, lT, dq, dkT)
+        return dq + dkT.transpose(-1, -2), None, None, None, None, None
+
+
+def landmark_inverse(lmk: torch.Tensor, scale: float, iters: int, init_mode: int = INIT_REFERENCE,
+                     reg: float | None = None, precision: int = PREC_SPLIT3) -> torch.Tensor:
+    """Inverse of the landmark kernel matrix exp(scale * cdist_1(L, L)) for fp32 L [B,H,M,D], M <= 128,
+    D <= 128, in one kernel (the matrix is never stored)."""
+    if reg is None:
+        reg = 0.01 if init_mode == INIT_REFERENCE else 0.0
+    return LandmarkInverseFn.apply(lmk, scale, iters, init_mode, reg, precision)
+
+
 def newton_residual(mat: torch.Tensor, inv: torch.Tensor, reg: float = 0.0) -> torch.Tensor:
     """||(A + reg I) X - I||_F per matrix, shape [B,H]."""
     res = torch.empty(mat.shape[0], mat.shape[1], device=mat.device,

@@ -68,3 +68,20 @@ def test_module(cuda):
     y = m(x)
     y.sum().backward()
     assert y.shape == x.shape and x.grad is not None
+
+
+def test_landmark_inverse_autograd_matches_composition(cuda):
+    """The fused landmark inverse and its backward agree with laplace_kernel
+    followed by newton_inverse (same forward bits; gradients to rounding)."""
+    from laplacianformer_b200.ops import landmark_inverse, laplace_kernel, newton_inverse
+
+    g = torch.Generator().manual_seed(5)
+    L = torch.randn(2, 2, 49, 64, generator=g).to(cuda)
+    G = torch.randn(2, 2, 49, 49, generator=g).to(cuda)
+    L1, L2 = L.clone().requires_grad_(), L.clone().requires_grad_()
+    x1 = landmark_inverse(L1, -0.125, 8)
+    x2 = newton_inverse(laplace_kernel(L2, L2.transpose(-1, -2).contiguous(), -0.125), 8)
+    assert torch.equal(x1, x2)
+    (x1 * G).sum().backward()
+    (x2 * G).sum().backward()
+    torch.testing.assert_close(L1.grad, L2.grad, rtol=1e-4, atol=1e-4)
