@@ -885,7 +885,10 @@ lsub_bwd_fast_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* 
 }
 
 // dKT of every (b,h) that the flat backward split over several CTAs: the
-// sum of their workspace slots in CTA order (bitwise reproducible).
+// sum of their workspace slots in CTA order (bitwise reproducible).  grid =
+// (bh, element blocks): one element per thread; the slot loop keeps four
+// independent partial sums (slots c0+4t+r go to partial r) that are combined
+// in a fixed order, so the loads of a long slot list overlap.
 template <typename T>
 __global__ void __launch_bounds__(kThreads)
 lsub_bwd_dk_finalize(const float* __restrict__ ws, T* __restrict__ dk, int d, int m, int64_t U, int64_t P) {
@@ -894,14 +897,24 @@ lsub_bwd_dk_finalize(const float* __restrict__ ws, T* __restrict__ dk, int d, in
     const int64_t c0 = first / P, c1 = last / P;
     if (c0 == c1) return;
     const int64_t dm = (int64_t)d * m;
-    for (int64_t e = threadIdx.x; e < dm; e += kThreads) {
-        float acc = 0.0f;
-        for (int64_t c = c0; c <= c1; ++c) {
-            const int64_t slot = 2 * c + (c * P >= first ? 0 : 1);
-            acc += ws[slot * dm + e];
-        }
-        dk[b * dm + e] = Elem<T>::store(acc);
+    const int64_t e = (int64_t)blockIdx.y * kThreads + threadIdx.x;
+    if (e >= dm) return;
+    auto slot_val = [&](int64_t c) {
+        const int64_t slot = 2 * c + (c * P >= first ? 0 : 1);
+        return ws[slot * dm + e];
+    };
+    float p0 = 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f;
+    int64_t c = c0;
+    for (; c + 3 <= c1; c += 4) {
+        p0 += slot_val(c);
+        p1 += slot_val(c + 1);
+        p2 += slot_val(c + 2);
+        p3 += slot_val(c + 3);
     }
+    if (c <= c1) p0 += slot_val(c);
+    if (c + 1 <= c1) p1 += slot_val(c + 1);
+    if (c + 2 <= c1) p2 += slot_val(c + 2);
+    dk[b * dm + e] = Elem<T>::store((p0 + p1) + (p2 + p3));
 }
 
 template <typename T, int MB, bool DQ, bool DK>
@@ -983,7 +996,8 @@ int launch_bwd_flat(const T* g, const T* q, const T* kT, T* dq, T* dk, int64_t b
     int rc = check_launch("lsub_bwd_fast_kernel");
     if (rc) return rc;
     if (bh > 0x7fffffff) { set_error("b*h too large"); return LF_ERR_UNSUPPORTED; }
-    lsub_bwd_dk_finalize<T><<<(unsigned)bh, kThreads, 0, st>>>(ws, dk, (int)d, (int)m, geo.U, geo.P);
+    const unsigned eblocks = (unsigned)((d * m + kThreads - 1) / kThreads);
+    lsub_bwd_dk_finalize<T><<<dim3((unsigned)bh, eblocks, 1), kThreads, 0, st>>>(ws, dk, (int)d, (int)m, geo.U, geo.P);
     return check_launch("lsub_bwd_dk_finalize");
 }
 
