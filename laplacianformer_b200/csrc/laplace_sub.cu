@@ -146,7 +146,7 @@ __device__ __forceinline__ A fwd_epilogue(A acc, A escale, bool do_exp) {
 template <typename T, int TM, int MC, int DR>
 __global__ void __launch_bounds__(kThreads)
 lsub_fwd_kernel(const T* __restrict__ q, const T* __restrict__ kT, T* __restrict__ s,
-                int n, int m, int d, int tiles_per_bh, bool vec, bool stage_out,
+                int n, int m, int d, int tiles_per_bh, bool vec, int gw,
                 typename Elem<T>::acc escale, bool do_exp) {
     using A = typename Elem<T>::acc;
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -154,9 +154,11 @@ lsub_fwd_kernel(const T* __restrict__ q, const T* __restrict__ kT, T* __restrict
     const int d16 = (d + 15) & ~15;
     const int DP = d16 > DR ? ((d + DR - 1) / DR) * DR : DR;
     const int MP = ((m + MC - 1) / MC) * MC;
-    // Output tile [kThreads*TM][m] in the storage type, after ks (16-byte
-    // aligned); written row-wise by the lanes, copied out as one contiguous
-    // run of S with 16-byte stores.
+    // Output tile [kThreads*TM][gw] in the storage type, after ks (16-byte
+    // aligned), gw = m or a multiple of MC (landmark groups of gw columns
+    // when the whole tile would not fit); written row-wise by the lanes and
+    // copied out with 16-byte stores: one contiguous run of S when gw = m,
+    // row segments of gw columns otherwise.  gw = 0: direct stores.
     T* so = reinterpret_cast<T*>(smem_raw + (((size_t)MP * DP * sizeof(A) + 15) & ~(size_t)15));
     const bool single = d <= DR;
 
@@ -209,6 +211,9 @@ lsub_fwd_kernel(const T* __restrict__ q, const T* __restrict__ kT, T* __restrict
     };
     if (single) load_q(0);
 
+    int g0 = 0;  // first landmark of the staged group
+    const int64_t trow = (int64_t)tile * (kThreads * TM);
+    const int64_t rows = (n - trow) < (int64_t)(kThreads * TM) ? (n - trow) : (int64_t)(kThreads * TM);
     for (int mc = 0; mc < m; mc += MC) {
         A acc[TM][MC];
 #pragma unroll
@@ -227,8 +232,8 @@ lsub_fwd_kernel(const T* __restrict__ q, const T* __restrict__ kT, T* __restrict
         }
 #pragma unroll
         for (int r = 0; r < TM; ++r) {
-            if (stage_out) {
-                T* out = so + (threadIdx.x + kThreads * r) * m + mc;
+            if (gw) {
+                T* out = so + (threadIdx.x + kThreads * r) * gw + (mc - g0);
 #pragma unroll
                 for (int j = 0; j < MC; ++j)
                     if (mc + j < m) out[j] = Elem<T>::store(fwd_epilogue(acc[r][j], escale, do_exp));
@@ -241,24 +246,47 @@ lsub_fwd_kernel(const T* __restrict__ q, const T* __restrict__ kT, T* __restrict
             for (int j = 0; j < MC; ++j)
                 if (mc + j < m) out[j] = Elem<T>::store(fwd_epilogue(acc[r][j], escale, do_exp));
         }
+        if (gw && (mc + MC >= g0 + gw || mc + MC >= m)) {
+            __syncthreads();
+            const int w = (m - g0) < gw ? (m - g0) : gw;
+            constexpr int V = 16 / sizeof(T);
+            if (w == m) {
+                // the tile's rows are one contiguous run of S
+                const int64_t cnt = rows * m;
+                T* dst = Sb + trow * m;
+                int64_t head = 0;
+                if ((reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+                    const int64_t nv = cnt / V;
+                    const uint4* src4 = reinterpret_cast<const uint4*>(so);
+                    uint4* dst4 = reinterpret_cast<uint4*>(dst);
+                    for (int64_t e = threadIdx.x; e < nv; e += kThreads) dst4[e] = src4[e];
+                    head = nv * V;
+                }
+                for (int64_t e = head + threadIdx.x; e < cnt; e += kThreads) dst[e] = so[e];
+            } else {
+                T* dst = Sb + trow * m + g0;
+                const bool v16 = (w % V == 0) && (m % V == 0) && (gw % V == 0) &&
+                                 (reinterpret_cast<uintptr_t>(dst) & 15) == 0;
+                if (v16) {
+                    const int U = w / V;
+                    for (int64_t e = threadIdx.x; e < rows * U; e += kThreads) {
+                        const int64_t r = e / U;
+                        const int u = (int)(e - r * U);
+                        *reinterpret_cast<uint4*>(dst + r * m + u * V) =
+                            *reinterpret_cast<const uint4*>(so + r * gw + u * V);
+                    }
+                } else {
+                    for (int64_t e = threadIdx.x; e < rows * w; e += kThreads) {
+                        const int64_t r = e / w;
+                        const int cc = (int)(e - r * w);
+                        dst[r * m + cc] = so[r * gw + cc];
+                    }
+                }
+            }
+            __syncthreads();
+            g0 += gw;
+        }
     }
-    if (!stage_out) return;
-    __syncthreads();
-    // The tile's rows are contiguous in S: copy valid_rows*m elements.
-    const int64_t trow = (int64_t)tile * (kThreads * TM);
-    const int64_t rows = (n - trow) < (int64_t)(kThreads * TM) ? (n - trow) : (int64_t)(kThreads * TM);
-    const int64_t cnt = rows * m;
-    T* dst = Sb + trow * m;
-    constexpr int V = 16 / sizeof(T);
-    int64_t head = 0;
-    if ((reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
-        const int64_t nv = cnt / V;
-        const uint4* src4 = reinterpret_cast<const uint4*>(so);
-        uint4* dst4 = reinterpret_cast<uint4*>(dst);
-        for (int64_t e = threadIdx.x; e < nv; e += kThreads) dst4[e] = src4[e];
-        head = nv * V;
-    }
-    for (int64_t e = head + threadIdx.x; e < cnt; e += kThreads) dst[e] = so[e];
 }
 
 // Landmark chunk per thread: the MC in 4..8 that pads m the least.
@@ -281,18 +309,25 @@ size_t fwd_smem(int64_t m, int64_t d) {
     return (size_t)MP * DP * sizeof(A);
 }
 
-// Bytes of the staged output tile, or 0 when S is stored directly (tiles
-// above kStageMax would cost occupancy).
+// Landmark columns of the staged output tile: all m when the tile fits in
+// kStageMax bytes (more would cost occupancy), else the widest multiple of MC
+// that does (landmark groups); 0 (direct stores) below 2*MC columns.
 constexpr size_t kStageMax = 64 * 1024;
-template <typename T, int TM>
+template <typename T, int TM, int MC>
+int fwd_stage_width(int64_t m) {
+    const size_t row_bytes = (size_t)kThreads * TM * sizeof(T);
+    if ((size_t)m * row_bytes <= kStageMax) return (int)m;
+    const int64_t w = (int64_t)(kStageMax / row_bytes) / MC * MC;
+    return w >= 2 * MC ? (int)w : 0;
+}
+template <typename T, int TM, int MC>
 size_t fwd_stage_bytes(int64_t m) {
-    size_t b = (size_t)kThreads * TM * m * sizeof(T);
-    return b <= kStageMax ? b : 0;
+    return (size_t)kThreads * TM * fwd_stage_width<T, TM, MC>(m) * sizeof(T);
 }
 
 template <typename T, int TM, int MC, int DR>
 size_t fwd_smem_total(int64_t m, int64_t d) {
-    size_t st = fwd_stage_bytes<T, TM>(m);
+    size_t st = fwd_stage_bytes<T, TM, MC>(m);
     size_t ks = fwd_smem<T, TM, MC, DR>(m, d);
     return st ? ((ks + 15) & ~(size_t)15) + st : ks;
 }
@@ -301,8 +336,11 @@ template <typename T, int TM, int MC, int DR>
 int launch_fwd_mc(const T* q, const T* kT, T* s, int64_t bh, int64_t n, int64_t m, int64_t d,
                   cudaStream_t st, double escale, bool do_exp) {
     size_t smem = fwd_smem_total<T, TM, MC, DR>(m, d);
-    const bool stage = fwd_stage_bytes<T, TM>(m) != 0 && smem <= (size_t)max_optin_smem();
-    if (!stage) smem = fwd_smem<T, TM, MC, DR>(m, d);
+    int gw = fwd_stage_width<T, TM, MC>(m);
+    if (gw == 0 || smem > (size_t)max_optin_smem()) {
+        gw = 0;
+        smem = fwd_smem<T, TM, MC, DR>(m, d);
+    }
     if (smem > (size_t)max_optin_smem()) {
         set_error("LaplaceSubtraction forward: m*d = %lld*%lld needs %zu bytes of shared memory",
                   (long long)m, (long long)d, smem);
@@ -315,7 +353,7 @@ int launch_fwd_mc(const T* q, const T* kT, T* s, int64_t bh, int64_t n, int64_t 
     int64_t blocks = bh * tiles;
     if (blocks > 0x7fffffff) { set_error("too many blocks"); return LF_ERR_UNSUPPORTED; }
     bool vec = (d % 16 == 0) && aligned(q, 16);
-    kern<<<(unsigned)blocks, kThreads, smem, st>>>(q, kT, s, (int)n, (int)m, (int)d, tiles, vec, stage,
+    kern<<<(unsigned)blocks, kThreads, smem, st>>>(q, kT, s, (int)n, (int)m, (int)d, tiles, vec, gw,
                                                    (typename Elem<T>::acc)escale, do_exp);
     return check_launch("lsub_fwd_kernel");
 }
