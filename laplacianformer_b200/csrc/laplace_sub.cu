@@ -1168,14 +1168,17 @@ lsub_bwd_wide_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* 
                 const A qv = qs[i * CW + cl];
                 const A* grow = gs + i * MPT + j0;
                 A dqa = A(0);
+                [[maybe_unused]] float dq4[4] = {0.f, 0.f, 0.f, 0.f};
+                [[maybe_unused]] unsigned long long qq = 0;
+                if constexpr (sizeof(A) == 4) asm("mov.b64 %0, {%1, %1};" : "=l"(qq) : "f"(qv));
 #pragma unroll
                 for (int j4 = 0; j4 < MB; j4 += 4) {
                     A gv[4];
                     if constexpr (sizeof(A) == 4) {
                         float4 t4 = *reinterpret_cast<const float4*>(grow + j4);
                         gv[0] = t4.x; gv[1] = t4.y; gv[2] = t4.z; gv[3] = t4.w;
-                        bwd_quad<true, true>(qv, kreg[j4], kreg[j4 + 1], kreg[j4 + 2], kreg[j4 + 3], gv, dqa,
-                                             dka[j4], dka[j4 + 1], dka[j4 + 2], dka[j4 + 3]);
+                        bwd_quad_x2(qq, kreg[j4], kreg[j4 + 1], kreg[j4 + 2], kreg[j4 + 3], gv, dq4,
+                                    dka[j4], dka[j4 + 1], dka[j4 + 2], dka[j4 + 3]);
                     } else {
 #pragma unroll
                         for (int e = 0; e < 4; ++e) {
@@ -1186,6 +1189,7 @@ lsub_bwd_wide_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* 
                         }
                     }
                 }
+                if constexpr (sizeof(A) == 4) dqa = (dq4[0] + dq4[1]) + (dq4[2] + dq4[3]);
                 dqp[(mcb * RC + i) * CW + cl] = dqa;
             }
         }
