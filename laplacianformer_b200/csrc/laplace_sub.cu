@@ -359,8 +359,8 @@ int launch_fwd_mc(const T* q, const T* kT, T* s, int64_t bh, int64_t n, int64_t 
 }
 
 // Two rows per thread amortise each landmark load over more terms; one row
-// per thread halves the CTA's rows.  Take one row only when that fills the
-// last wave of CTAs clearly better.
+// per thread halves the CTA's rows (twice the CTAs).  The choice compares
+// the estimated times of the two grids.
 template <typename T, int MC, int DR>
 int launch_fwd_tm(const T* Q, const T* K, T* S, int64_t bh, int64_t n, int64_t m, int64_t d, cudaStream_t st,
                  double escale, bool do_exp) {
@@ -372,9 +372,15 @@ int launch_fwd_tm(const T* Q, const T* K, T* S, int64_t bh, int64_t n, int64_t m
             auto k2 = lsub_fwd_kernel<T, 2, MC, DR>;
             if (smem1 > 48 * 1024) cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem1);
             if (smem2 > 48 * 1024) cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem2);
-            double e1 = wave_efficiency(bh * ((n + kThreads - 1) / kThreads), cta_slots(k1, smem1));
-            double e2 = wave_efficiency(bh * ((n + 2 * kThreads - 1) / (2 * kThreads)), cta_slots(k2, smem2));
-            if (e1 > e2 + 0.05) return launch_fwd_mc<T, 1, MC, DR>(Q, K, S, bh, n, m, d, st, escale, do_exp);
+            // Estimated time in one-row CTA times: waves x rows per thread
+            // (a two-row CTA costs ~1.8 one-row CTAs: the landmark loads are
+            // shared).  Small grids (under one wave) thus take one row.
+            const int64_t s1 = cta_slots(k1, smem1), s2 = cta_slots(k2, smem2);
+            const int64_t n1 = bh * ((n + kThreads - 1) / kThreads);
+            const int64_t n2 = bh * ((n + 2 * kThreads - 1) / (2 * kThreads));
+            const double t1 = (double)((n1 + s1 - 1) / s1);
+            const double t2 = 1.8 * (double)((n2 + s2 - 1) / s2);
+            if (t1 <= t2) return launch_fwd_mc<T, 1, MC, DR>(Q, K, S, bh, n, m, d, st, escale, do_exp);
         }
         return launch_fwd_mc<T, 2, MC, DR>(Q, K, S, bh, n, m, d, st, escale, do_exp);
     } else {
