@@ -78,3 +78,70 @@ def run_sharded(fn: Callable[..., Sequence[torch.Tensor]], inputs: Sequence[torc
     if not gather or world == 1:
         return outs
     return [all_gather_bh(o, total, group) for o in outs]
+
+
+def run_sharded_overlapped(fn: Callable[..., Sequence[torch.Tensor]], inputs: Sequence[torch.Tensor],
+                           chunks: int = 4, group=None) -> list[torch.Tensor]:
+    """run_sharded(..., gather=True) with the all-gather overlapped with compute.
+
+    This rank's B*H slice is cut into `chunks` pieces of c = ceil(ceil(B*H /
+    world) / chunks) slices (every rank uses the same c, padding its last
+    pieces).  Piece i is computed, then its outputs are all-gathered with an
+    asynchronous collective while piece i+1 is computed (NCCL runs the
+    gather on its own stream after the work already queued on the current
+    stream; gloo on its own thread).  Returns the outputs as [B*H, ...], the
+    same as run_sharded.
+    """
+    world = dist.get_world_size(group) if dist.is_initialized() else 1
+    rank = dist.get_rank(group) if dist.is_initialized() else 0
+    total = inputs[0].shape[0] * inputs[0].shape[1]
+    for t in inputs:
+        if t.shape[0] * t.shape[1] != total:
+            raise ValueError("inputs must share B*H")
+    if world == 1:
+        return run_sharded(fn, inputs, gather=False, group=group)
+    local = [local_slice(t, world, rank) for t in inputs]
+    n_local = local[0].shape[0]
+    per_rank = -(-total // world)
+    chunks = max(1, min(chunks, per_rank))
+    c = -(-per_rank // chunks)
+    pending = []  # (piece index, gathered buffers, works)
+    for i in range(chunks):
+        a, b = min(i * c, n_local), min((i + 1) * c, n_local)
+        if b > a:
+            outs = [flatten_bh(o) for o in fn(*[t[a:b].unsqueeze(0) for t in local])]
+        else:  # this rank has no slices left for this piece: gather zeros
+            shapes = pending[0][3] if pending else None
+            if shapes is None:
+                probe = fn(*[t[:1].unsqueeze(0) for t in local])
+                shapes = [(tuple(o.shape[2:]), o.dtype, o.device) for o in probe]
+            outs = [torch.zeros((0,) + s, dtype=dt, device=dv) for s, dt, dv in shapes]
+        sends, bufs, works = [], [], []
+        for o in outs:
+            send = o
+            if o.shape[0] != c:
+                send = o.new_zeros((c,) + tuple(o.shape[1:]))
+                send[: o.shape[0]] = o
+            buf = o.new_empty((c * world,) + tuple(o.shape[1:]))
+            works.append(dist.all_gather_into_tensor(buf, send.contiguous(), group=group, async_op=True))
+            sends.append(send)
+            bufs.append(buf)
+        shapes = [(tuple(o.shape[1:]), o.dtype, o.device) for o in outs]
+        pending.append((i, bufs, works, shapes, sends))
+    for _, _, works, _, _ in pending:
+        for w in works:
+            w.wait()
+    # assemble: rank r's piece i holds its slices [i*c, i*c + len) at global start(r) + i*c
+    n_out = len(pending[0][1])
+    result = []
+    for k in range(n_out):
+        ref = pending[0][1][k]
+        out = ref.new_empty((total,) + tuple(ref.shape[1:]))
+        for i, bufs, _, _, _ in pending:
+            for r in range(world):
+                s, e = shard_bounds(total, world, r)
+                a, b = min(s + i * c, e), min(s + (i + 1) * c, e)
+                if b > a:
+                    out[a:b] = bufs[k][r * c: r * c + (b - a)]
+        result.append(out)
+    return result

@@ -127,6 +127,36 @@ def _leaver(rank, world, port, result_q):
         os._exit(0)
 
 
+def _overlap_worker(rank, world, port, bh, chunks, result_q):
+    _init(rank, world, port)
+    try:
+        from laplacianformer_b200.sharding import run_sharded_overlapped
+
+        g = torch.Generator().manual_seed(1)
+        q = torch.randn(1, bh, 12, 4, generator=g)
+        k = torch.randn(1, bh, 4, 3, generator=g)
+
+        def fn(ql, kl):
+            d = (ql.unsqueeze(-1) - kl.unsqueeze(-3)).abs().sum(-2)  # [1, b, 12, 3]
+            return d, ql * 2.0
+
+        ref = run_sharded(fn, [q, k])
+        got = run_sharded_overlapped(fn, [q, k], chunks=chunks)
+        ok = all(torch.equal(a, b) for a, b in zip(ref, got)) and got[0].shape[0] == bh
+        result_q.put((rank, bool(ok)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("bh,chunks", [(8, 3), (7, 2), (3, 4), (5, 1)])
+def test_overlapped_gather_matches_run_sharded(bh, chunks):
+    q, procs = _spawn(_overlap_worker, (bh, chunks))
+    res = dict(q.get(timeout=180) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    assert res == {0: True, 1: True}
+
+
 def test_rank_leaving_before_collective_raises():
     q, procs = _spawn(_leaver)
     rank, what = q.get(timeout=180)
