@@ -342,12 +342,49 @@ def run_config5(args, rank, world, dev):
     X = torch.empty_like(sll)
     sigma = math.sqrt(D)
 
-    def step():
-        capi.laplace_sub_fwd(q, kT, s)
-        capi.laplace_sub_bwd(ds, q, kT, dq, dk)
+    gather = args.gather if world > 1 else "none"
+    gbufs = None
+    if gather != "none":
+        # replicated dQ, dK^T and X on every rank (S stays sharded: gathering
+        # it would move more bytes over NVLink than the sharded compute saves)
+        gbufs = [torch.empty((world,) + tuple(t.shape), device=dev, dtype=t.dtype) for t in (dq, dk, X)]
+    pieces = 4 if gather == "overlap" else 1
+    per = -(-bh // pieces)
+    bounds = [(i * per, min(bh, (i + 1) * per)) for i in range(pieces)]
+    pbufs = []
+    if gather == "overlap":  # one receive buffer per piece and output
+        pbufs = [[torch.empty((world, b - a) + tuple(t.shape[2:]), device=dev, dtype=t.dtype) for t in (dq, dk, X)]
+                 for a, b in bounds]
+
+    def distances(a, b):
+        sl = slice(a, b)
+        capi.laplace_sub_fwd(q[:, sl], kT[:, sl], s[:, sl])
+        capi.laplace_sub_bwd(ds[:, sl], q[:, sl], kT[:, sl], dq[:, sl], dk[:, sl])
+
+    def inverse():
         capi.laplace_sub_fwd(Lf, LfT, sll)
         A = torch.exp(sll * (-1.0 / sigma))
         capi.newton_inverse_fwd(A, 10, out=X)
+
+    def step():
+        if gather == "none":
+            distances(0, bh)
+            inverse()
+            return
+        works = []
+        for i, (a, b) in enumerate(bounds):
+            distances(a, b)
+            if gather == "overlap":  # piece i's dQ/dK^T cross NVLink while piece i+1 (and the inverse) compute
+                for t, buf in zip((dq, dk), pbufs[i][:2]):
+                    works.append(torch.distributed.all_gather_into_tensor(buf, t[0, a:b], async_op=True))
+        inverse()
+        if gather == "overlap":
+            works.append(torch.distributed.all_gather_into_tensor(gbufs[2], X, async_op=True))
+        if gather == "after":
+            for t, buf in zip((dq, dk, X), gbufs):
+                torch.distributed.all_gather_into_tensor(buf, t)
+        for w in works:
+            w.wait()
 
     times = time_steps(step, args.steps, args.warmup, flush, stream)
     ms = max_over_ranks(statistics.mean(times))
@@ -357,7 +394,8 @@ def run_config5(args, rank, world, dev):
         "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded N(0,1), configuration-5 shapes)",
         "config": {"workload": f"config5 N={N}: LaplaceSub fwd+bwd bf16 (M=256, D=64) + NewtonInverse 256x256 fp32 x10",
-                   "global_batch": B, "heads": H, "seq_len": N, "parallelism": f"bh-shard x{world} (strong), no collective",
+                   "global_batch": B, "heads": H, "seq_len": N, "parallelism": f"bh-shard x{world} (strong), " + ("no collective" if gather == "none" else
+                                   f"dQ/dK/X all-gathered ({gather})"),
                    "l2": "inputs larger than L2" if N >= 16384 else "flushed between timed steps"},
         "newton_matrices_per_s": B * H / (ms / 1e3),
     }
@@ -488,6 +526,8 @@ def main():
     ap.add_argument("--ns-batch", type=int, default=4096)
     ap.add_argument("--workload", choices=["config2", "config5"], default="config2")
     ap.add_argument("--n-tokens", type=int, default=16384, help="configuration-5 sequence length")
+    ap.add_argument("--gather", choices=["none", "after", "overlap"], default="none",
+                    help="configuration 5 with N>1: all-gather dQ, dK^T and X after the compute or overlapped per piece")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
