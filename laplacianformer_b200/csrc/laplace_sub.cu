@@ -48,9 +48,25 @@ inline double wave_efficiency(int64_t total, int64_t slots) {
 
 template <typename K>
 int64_t cta_slots(K kern, size_t smem) {
+    // The occupancy query costs microseconds of host time per launch; cache
+    // the last answer (kernel, device, shared-memory size).  Kernels of one
+    // signature share this instantiation, so the kernel is part of the key.
+    static std::mutex mu;
+    static const void* c_kern = nullptr;
+    static int c_dev = -1, c_per_sm = 0;
+    static size_t c_smem = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const void* kp = reinterpret_cast<const void*>(kern);
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (kp == c_kern && dev == c_dev && smem == c_smem) return (int64_t)c_per_sm * num_sms();
+    }
     int per_sm = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem) != cudaSuccess || per_sm < 1)
         per_sm = 1;
+    std::lock_guard<std::mutex> lock(mu);
+    c_kern = kp; c_dev = dev; c_smem = smem; c_per_sm = per_sm;
     return (int64_t)per_sm * num_sms();
 }
 
