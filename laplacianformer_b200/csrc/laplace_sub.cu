@@ -806,6 +806,7 @@ lsub_bwd_fast_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* 
     for (int k = 0; k < CPT; ++k) colp[k] = A(0);
 
     A pg[CPT], pq[8];
+    const bool qvec = (d == 32) && ((reinterpret_cast<uintptr_t>(q) & 15) == 0);
     auto load_chunk = [&](int64_t rc) {
         const int64_t row = rc + sr;
         const bool ok = row < r_end;
@@ -813,8 +814,22 @@ lsub_bwd_fast_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* 
 #pragma unroll
         for (int k = 0; k < CPT; ++k) pg[k] = (ok && sq * CPT + k < m) ? Elem<T>::load(grow[k]) : A(0);
         const T* qrow = Qb + row * d + sq * 8;
+        if (qvec && ok) {  // d == 32, 16-byte aligned rows: the eight values in one or two 16-byte loads
+            if constexpr (sizeof(T) == 4) {
+                const float4 a0 = __ldg(reinterpret_cast<const float4*>(qrow));
+                const float4 a1 = __ldg(reinterpret_cast<const float4*>(qrow) + 1);
+                pq[0] = a0.x; pq[1] = a0.y; pq[2] = a0.z; pq[3] = a0.w;
+                pq[4] = a1.x; pq[5] = a1.y; pq[6] = a1.z; pq[7] = a1.w;
+            } else {
+                const uint4 u = __ldg(reinterpret_cast<const uint4*>(qrow));
+                const T* h = reinterpret_cast<const T*>(&u);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) pq[k] = (ok && sq * 8 + k < d) ? Elem<T>::load(qrow[k]) : A(0);
+                for (int k = 0; k < 8; ++k) pq[k] = Elem<T>::load(h[k]);
+            }
+        } else {
+#pragma unroll
+            for (int k = 0; k < 8; ++k) pq[k] = (ok && sq * 8 + k < d) ? Elem<T>::load(qrow[k]) : A(0);
+        }
     };
     if (r_begin < r_end) load_chunk(r_begin);
 
