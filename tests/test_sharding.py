@@ -84,12 +84,31 @@ def _spawn(target, extra=()):
     return q, procs
 
 
+def _run_pair(target, extra=(), timeout=120):
+    """Run two gloo ranks and collect {rank: result}.  A rendezvous on a port
+    that another process grabbed between _free_port and the bind can hang;
+    such an attempt is terminated and retried once on a fresh port."""
+    import queue as _queue
+
+    for attempt in range(2):
+        q, procs = _spawn(target, extra)
+        try:
+            res = dict(q.get(timeout=timeout) for _ in procs)
+        except _queue.Empty:
+            for p in procs:
+                p.terminate()
+                p.join(timeout=10)
+            if attempt == 1:
+                raise
+            continue
+        for p in procs:
+            p.join(timeout=60)
+        return res
+
+
 @pytest.mark.parametrize("bh", [8, 6])
 def test_two_gloo_ranks_match_single_process(bh):
-    q, procs = _spawn(_worker, (bh,))
-    res = dict(q.get(timeout=180) for _ in procs)
-    for p in procs:
-        p.join(timeout=60)
+    res = _run_pair(_worker, (bh,))
     assert res == {0: True, 1: True}
 
 
@@ -105,10 +124,7 @@ def _gather_uneven(rank, world, port, result_q):
 
 
 def test_uneven_all_gather():
-    q, procs = _spawn(_gather_uneven)
-    res = dict(q.get(timeout=180) for _ in procs)
-    for p in procs:
-        p.join(timeout=60)
+    res = _run_pair(_gather_uneven)
     assert res == {0: True, 1: True}
 
 
@@ -150,10 +166,7 @@ def _overlap_worker(rank, world, port, bh, chunks, result_q):
 
 @pytest.mark.parametrize("bh,chunks", [(8, 3), (7, 2), (3, 4), (5, 1)])
 def test_overlapped_gather_matches_run_sharded(bh, chunks):
-    q, procs = _spawn(_overlap_worker, (bh, chunks))
-    res = dict(q.get(timeout=180) for _ in procs)
-    for p in procs:
-        p.join(timeout=60)
+    res = _run_pair(_overlap_worker, (bh, chunks))
     assert res == {0: True, 1: True}
 
 
