@@ -167,7 +167,8 @@ LF_API int lf_laplace_sub_bwd_ws(const void* g, const void* q, const void* kT,
    lf_laplace_sub_bwd_workspace_size exceeds 2 MiB are rejected with
    LF_ERR_UNSUPPORTED; shapes with size 0 run lf_laplace_sub_bwd.  The first
    call on a device looks up the array's device address (cudaGetSymbolAddress)
-   with that device current; make that first call before any stream capture.
+   with that device current; make that first call before any stream capture
+   (a failed lookup is reported as LF_ERR_CUDA and retried by the next call).
    All calls share the one array and each overwrites what it reads (nothing
    needs to start at zero), so calls that can overlap on the GPU (different
    streams or host threads) race: serialise them.  No counterpart in the

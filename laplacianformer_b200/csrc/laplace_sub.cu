@@ -27,7 +27,9 @@
 #include <cooperative_groups.h>
 #include <stdlib.h>
 
+#include <map>
 #include <mutex>
+#include <tuple>
 
 #include "lf_common.cuh"
 
@@ -48,25 +50,25 @@ inline double wave_efficiency(int64_t total, int64_t slots) {
 
 template <typename K>
 int64_t cta_slots(K kern, size_t smem) {
-    // The occupancy query costs microseconds of host time per launch; cache
-    // the last answer (kernel, device, shared-memory size).  Kernels of one
-    // signature share this instantiation, so the kernel is part of the key.
+    // The occupancy query costs microseconds of host time per launch, so the
+    // answer is cached per (kernel, device, shared-memory size).  Launchers
+    // that compare two kernels query both on every call, so the cache keeps
+    // every key rather than only the last one.
     static std::mutex mu;
-    static const void* c_kern = nullptr;
-    static int c_dev = -1, c_per_sm = 0;
-    static size_t c_smem = 0;
+    static std::map<std::tuple<const void*, int, size_t>, int> cache;
     int dev = 0;
     cudaGetDevice(&dev);
-    const void* kp = reinterpret_cast<const void*>(kern);
+    const auto key = std::make_tuple(reinterpret_cast<const void*>(kern), dev, smem);
     {
         std::lock_guard<std::mutex> lock(mu);
-        if (kp == c_kern && dev == c_dev && smem == c_smem) return (int64_t)c_per_sm * num_sms();
+        auto it = cache.find(key);
+        if (it != cache.end()) return (int64_t)it->second * num_sms();
     }
     int per_sm = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem) != cudaSuccess || per_sm < 1)
         per_sm = 1;
     std::lock_guard<std::mutex> lock(mu);
-    c_kern = kp; c_dev = dev; c_smem = smem; c_per_sm = per_sm;
+    cache[key] = per_sm;
     return (int64_t)per_sm * num_sms();
 }
 
@@ -1686,16 +1688,23 @@ static __device__ __align__(256) float g_bwd_scratch[kNoAllocScratchBytes / size
 
 namespace {
 constexpr int kNoAllocMaxDev = 64;
-std::once_flag g_scratch_once[kNoAllocMaxDev];
+std::mutex g_scratch_mu;
 void* g_scratch_ptr[kNoAllocMaxDev];
-cudaError_t g_scratch_err[kNoAllocMaxDev];
 
 // In host code g_bwd_scratch names a host-side stand-in; the device address
-// is asked for once per device, with that device current.
-void scratch_setup(int dev) {
-    void* p = nullptr;
-    g_scratch_err[dev] = cudaGetSymbolAddress(&p, g_bwd_scratch);
-    g_scratch_ptr[dev] = (g_scratch_err[dev] == cudaSuccess) ? p : nullptr;
+// is asked for with the device current.  Only a successful lookup is kept, so
+// a failure (for example a first call made during stream capture) is
+// reported and the next call tries again.
+void* scratch_address(int dev, cudaError_t* err) {
+    std::lock_guard<std::mutex> lock(g_scratch_mu);
+    *err = cudaSuccess;
+    if (!g_scratch_ptr[dev]) {
+        void* p = nullptr;
+        *err = cudaGetSymbolAddress(&p, g_bwd_scratch);
+        if (*err == cudaSuccess) g_scratch_ptr[dev] = p;
+        else cudaGetLastError();  // the failed lookup must not leak into the next launch check
+    }
+    return g_scratch_ptr[dev];
 }
 }  // namespace
 
@@ -1721,14 +1730,14 @@ extern "C" int lf_laplace_sub_bwd_noalloc(const void* g, const void* q, const vo
         set_error("lf_laplace_sub_bwd_noalloc: no usable current device");
         return LF_ERR_CUDA;
     }
-    std::call_once(g_scratch_once[dev], scratch_setup, dev);
-    if (!g_scratch_ptr[dev]) {
-        set_error("lf_laplace_sub_bwd_noalloc: cudaGetSymbolAddress failed: %s",
-                  cudaGetErrorString(g_scratch_err[dev]));
+    cudaError_t err = cudaSuccess;
+    void* scratch = scratch_address(dev, &err);
+    if (!scratch) {
+        set_error("lf_laplace_sub_bwd_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(err));
         return LF_ERR_CUDA;
     }
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    LF_DISPATCH(dtype, T, return launch_bwd_flat_t<T>(g, q, kT, dq, dkT, bh, n, m, d, g_scratch_ptr[dev],
+    LF_DISPATCH(dtype, T, return launch_bwd_flat_t<T>(g, q, kT, dq, dkT, bh, n, m, d, scratch,
                                                       kNoAllocScratchBytes, nullptr, st));
     return LF_OK;
 }

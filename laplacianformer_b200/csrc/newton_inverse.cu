@@ -42,29 +42,13 @@ namespace lfb {
 // whose bounded wait expired.  Read and cleared by lf_device_status().
 __device__ int g_ns_status = 0;
 
-// Phase timestamps of CTA 0 for kernel development builds (-DLF_NS_TRACE);
-// compiled out otherwise.
-#ifdef LF_NS_TRACE
-__device__ long long g_ns_trace[16][32];
-#define NS_TRACE(it, k)                                                                          \
-    do {                                                                                         \
-        if (blockIdx.x == 0 && (threadIdx.x == 0 || threadIdx.x == 256) && (it) < 16)            \
-            g_ns_trace[it][(k) + (threadIdx.x ? 16 : 0)] = clock64();                            \
-    } while (0)
-#else
-#define NS_TRACE(it, k) \
-    do {                \
-    } while (0)
-#endif
-
 namespace {
 
-constexpr int kNsThreads = 512;
-constexpr int kTile = 128;                 // padded matrix size
+constexpr int kTcThreads = 256;            // 8 warps; two CTAs share an SM
+constexpr int kTile = 128;                 // padded matrix size (one tile)
 constexpr int kOpBytes = kTile * kTile * 2; // one fp16 operand (32 KB)
-constexpr bool kWInTmem = true;        // W operand of the second product in TMEM (else shared memory)
-constexpr bool kSplitW = false;        // W = V P as two N = 64 halves (true) or one N = 128 product
-constexpr int kTmemCols = 512;             // W and Y accumulators + fp32 V (384 used)
+constexpr int kTmemCols = 256;             // accumulator [0,128), P hi [128,192), P lo [192,256)
+constexpr int kLtChunk = 64;               // landmark channels staged per set-up pass
 
 // ---------------------------------------------------------------------------
 // PTX wrappers (tcgen05, mbarrier, fences)
@@ -85,23 +69,67 @@ __device__ __forceinline__ uint64_t global_ns() {
 
 // Returns true when the phase with the given parity has completed, false if
 // it has not completed within about two seconds (bounded wait; the caller
-// reports LF_ERR_TIMEOUT instead of hanging the GPU).
+// reports LF_ERR_TIMEOUT instead of hanging the GPU).  Each try_wait may
+// suspend the thread for up to 20 us until the phase completes, so waiting
+// warps do not spin on the issue slots the epilogue warps need.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns = 2000000000ull) {
     const uint32_t addr = smem_u32(bar);
-    const uint64_t t0 = global_ns();
+    uint64_t t0 = 0;
     for (uint32_t spin = 0;; ++spin) {
         uint32_t done;
         asm volatile(
             "{\n\t.reg .pred p;\n\t"
-            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
             "selp.u32 %0, 1, 0, p;\n\t}\n"
             : "=r"(done)
-            : "r"(addr), "r"(parity)
+            : "r"(addr), "r"(parity), "r"(20000u)
             : "memory");
         if (done) return true;
-        if ((spin & 255u) == 255u && global_ns() - t0 > limit_ns) return false;
+        if (spin == 0) t0 = global_ns();
+        else if (global_ns() - t0 > limit_ns) return false;
     }
 }
+
+// One lane of the calling (converged) warp returns true.
+__device__ __forceinline__ bool elect_one() {
+    uint32_t pred;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "elect.sync _|p, 0xffffffff;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(pred));
+    return pred != 0;
+}
+
+// Packed fp32 pairs (sm_100 f32x2 arithmetic: one issue slot per pair).
+__device__ __forceinline__ uint64_t pk2(float a, float b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void upk2(uint64_t v, float& a, float& b) { asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v)); }
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+__device__ __forceinline__ uint64_t sub2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+// fp16 pair of (lo, hi) = the two floats of v (first float in the low half).
+__device__ __forceinline__ __half2 cvt_h2(uint64_t v) {
+    float a, b;
+    upk2(v, a, b);
+    return __float22half2_rn(make_float2(a, b));
+}
+__device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<const uint32_t*>(&h); }
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -115,81 +143,65 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
 }
 
-// D[tmem] (+)= A[smem] * B[smem], kind::f16, cta_group::1.
-__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+// D[tmem] (+)= A[smem] * B[smem], kind::f16, cta_group::1, issued by the
+// lane with go != 0.  The whole warp executes the instruction (predicated),
+// so descriptors computed in converged code stay in uniform registers and
+// each MMA issues in a few cycles; an MMA inside a one-lane branch measured
+// about twice the tensor pipe's time per instruction.
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                        uint32_t accumulate, uint32_t go) {
     asm volatile(
-        "{\n\t.reg .pred p;\n\t"
+        "{\n\t.reg .pred p, q;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        "setp.ne.b32 q, %5, 0;\n\t"
+        "@q tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(go)
         : "memory");
 }
 // D[tmem] (+)= A[tmem] * B[smem], kind::f16: A is 128 lanes (rows) x K fp16
-// with consecutive K pairs packed in one 32-bit column.
-__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+// with consecutive K pairs packed in one 32-bit column (lower K in the low half).
+__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t accumulate, uint32_t go) {
     asm volatile(
-        "{\n\t.reg .pred p;\n\t"
+        "{\n\t.reg .pred p, q;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
-        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        "setp.ne.b32 q, %5, 0;\n\t"
+        "@q tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(go)
         : "memory");
 }
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-// 32 lanes x 32 consecutive 32-bit columns: thread i of the warp gets lane
-// (quadrant*32 + i), columns [col, col+32).
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+// 32 lanes x 16 consecutive 32-bit columns: thread i of the warp gets lane
+// (quadrant*32 + i), columns [col, col+16).
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     uint32_t* r = reinterpret_cast<uint32_t*>(v);
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
         : "r"(taddr));
-}
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
-    const uint32_t* r = reinterpret_cast<const uint32_t*>(v);
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
-        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
-        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
-        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
-        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),
-        "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]),
-        "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
-        : "memory");
-}
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
-        "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
-        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
-        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
-        : "memory");
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 // Ties registers written by tcgen05.ld to a point after tcgen05.wait::ld so
 // that the compiler cannot hoist their uses above the wait.
-__device__ __forceinline__ void reg_fence(float (&v)[32]) {
+template <int N>
+__device__ __forceinline__ void reg_fence(float (&v)[N]) {
 #pragma unroll
-    for (int i = 0; i < 32; ++i) asm volatile("" : "+f"(v[i]));
+    for (int i = 0; i < N; ++i) asm volatile("" : "+f"(v[i]));
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // ---------------------------------------------------------------------------
 // Operand layout: a 128x128 fp16 matrix X[r][c], row-major with the 128-byte
 // swizzle.  Columns [0,64) and [64,128) form two 16 KB blocks; row r of a
-// block is 128 bytes at r*128 and its 16-byte chunk k sits at chunk k^(r%8).
+// block is 128 bytes at r*128 and its 16-byte chunk k (columns 8k..8k+7 of
+// the block) sits at chunk k^(r%8).  The same bytes are a K-major A operand
+// and an MN-major B operand.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t op_chunk_offset(int r, int col8) {
-    // byte offset of the 16-byte chunk holding columns [8*col8, 8*col8+8) of row r
-    return (uint32_t)((col8 >> 3) * 16384 + r * 128 + (((col8 & 7) ^ (r & 7)) << 4));
-}
 
 // Shared-memory matrix descriptor (sm_100): start>>4 [0,14), LBO>>4 [16,30),
 // SBO>>4 [32,46), version 1 at bit 46, layout SWIZZLE_128B (2) at [61,64).
@@ -202,405 +214,520 @@ __device__ __forceinline__ uint64_t make_desc(uint32_t saddr, uint32_t lbo, uint
     d |= (uint64_t)2 << 61;
     return d;
 }
-// A operand (K-major view of the row-major layout), K step ks of 16 columns.
-__device__ __forceinline__ uint64_t desc_a(uint32_t base, int ks) {
-    return make_desc(base + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024);
-}
-// B operand (MN-major view: rows = k, contiguous columns = n), K step ks.
-__device__ __forceinline__ uint64_t desc_b(uint32_t base, int ks) {
-    return make_desc(base + ks * 2048, 16384, 1024);
-}
-// Power-of-two scale that maps max|x| into [2^14, 2^15); 1 for 0 or non-finite.
+// kind::f16 instruction descriptor: fp32 accumulator, fp16 A and B, A
+// K-major, B MN-major, N = M = 128.
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 16) | ((uint32_t)(kTile >> 3) << 17) | ((uint32_t)(kTile >> 4) << 24);
+
+// Power-of-two scale that maps max|x| into [2^14, 2^15); 1 for 0, negative
+// or non-finite input, 2^127 for subnormal input.  Built from the exponent
+// bits: a handful of integer instructions on the epilogues' critical path.
 __device__ __forceinline__ float split_scale(float mx) {
-    if (!(mx > 0.f) || !isfinite(mx)) return 1.f;
-    int e;
-    frexpf(mx, &e);  // mx = f * 2^e, f in [0.5, 1)
-    return ldexpf(1.f, 15 - e);
+    const uint32_t b = __float_as_uint(mx);
+    const int e = (int)((b >> 23) & 0xffu);  // biased exponent: mx in [2^(e-127), 2^(e-126))
+    if (!(mx > 0.f) || e == 0xff) return 1.f;
+    const int se = min(127 + 141 - e, 254);  // s = 2^(14 - (e - 127))
+    return __uint_as_float((uint32_t)se << 23);
 }
 
-__device__ __forceinline__ void split_store(unsigned char* hi_base, unsigned char* lo_base, int r,
-                                            int col0, const float (&v)[32], float s) {
-    // v holds columns [col0, col0+32) of row r (col0 a multiple of 32); stores
-    // hi = fp16(v*s) and lo = fp16(v*s - hi), two elements per conversion.
+__device__ __forceinline__ void sts128(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+
+// Row `r`, 64 columns of V * s into the operand buffers (vh_row: shared
+// address of the row's 64-column block in V hi; V lo follows V hi at
+// kOpBytes): hi always, lo = fp16(V*s - hi) when `lo` (16-byte swizzled
+// chunks, conflict-free across the 32 rows of a warp).  Returns max|hi|
+// (= max|V| s up to the fp16 rounding of hi).
+__device__ __forceinline__ float store_v(uint32_t vh_row, int rx, const float (&v)[64], float s, bool lo) {
+    const uint64_t ss = pk2(s, s);
+    __half2 hm0 = __float2half2_rn(0.f), hm1 = hm0;
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
+    for (int k = 0; k < 8; ++k) {
         uint32_t h[4], l[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-            const float2 xs = make_float2(v[8 * k + 2 * e] * s, v[8 * k + 2 * e + 1] * s);
-            const __half2 hh = __float22half2_rn(xs);
-            const float2 hb = __half22float2(hh);
-            const __half2 ll = __float22half2_rn(make_float2(xs.x - hb.x, xs.y - hb.y));
-            h[e] = *reinterpret_cast<const uint32_t*>(&hh);
-            l[e] = *reinterpret_cast<const uint32_t*>(&ll);
+            const uint64_t xs = mul2(pk2(v[8 * k + 2 * e], v[8 * k + 2 * e + 1]), ss);
+            const __half2 hh = cvt_h2(xs);
+            if (e & 1) hm1 = __hmax2(hm1, __habs2(hh));
+            else hm0 = __hmax2(hm0, __habs2(hh));
+            h[e] = h2u(hh);
+            if (lo) {
+                const float2 hb = __half22float2(hh);
+                l[e] = h2u(cvt_h2(sub2(xs, pk2(hb.x, hb.y))));
+            }
         }
-        uint32_t off = op_chunk_offset(r, (col0 >> 3) + k);
-        *reinterpret_cast<uint4*>(hi_base + off) = make_uint4(h[0], h[1], h[2], h[3]);
-        *reinterpret_cast<uint4*>(lo_base + off) = make_uint4(l[0], l[1], l[2], l[3]);
+        const uint32_t off = vh_row + ((k ^ rx) << 4);
+        sts128(off, h[0], h[1], h[2], h[3]);
+        if (lo) sts128(off + kOpBytes, l[0], l[1], l[2], l[3]);
     }
+    const __half2 hm = __hmax2(hm0, hm1);
+    return fmaxf(__low2float(hm), __high2float(hm));
 }
 
-__device__ __forceinline__ void named_sync(int id, int count) {
-    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
-}
-__device__ __forceinline__ void named_arrive(int id, int count) {
-    asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(count) : "memory");
-}
-
-// hi/lo fp16 split of 32 values into packed pairs (element 2i in the low half).
-__device__ __forceinline__ void split_pack(const float (&v)[32], float s, uint32_t (&h)[16], uint32_t (&l)[16]) {
+// G * sG for 16 accumulator columns (chunk j16 of the thread's 64) holding
+// H * sP * sV, stored as fp16 into the G operand: g = delta - H, so the scaled
+// value is acc * chs (+ sG on the diagonal) with chs = -sG/(sP sV).
+// DIAG: column j of the chunk is the diagonal for the lane with lane == j + joff.
+template <bool DIAG>
+__device__ __forceinline__ void g_store(const float (&a)[16], uint64_t chs2, float sG, int lane, int joff,
+                                        __half2& hm, uint32_t gh_row, int rx, int j16) {
 #pragma unroll
-    for (int e = 0; e < 16; ++e) {
-        const float2 xs = make_float2(v[2 * e] * s, v[2 * e + 1] * s);
-        const __half2 hh = __float22half2_rn(xs);
-        const float2 hb = __half22float2(hh);
-        const __half2 ll = __float22half2_rn(make_float2(xs.x - hb.x, xs.y - hb.y));
-        h[e] = *reinterpret_cast<const uint32_t*>(&hh);
-        l[e] = *reinterpret_cast<const uint32_t*>(&ll);
+    for (int q = 0; q < 2; ++q) {
+        uint32_t hp[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int j = 8 * q + 2 * e;
+            uint64_t g;
+            if (DIAG) g = fma2(pk2(a[j], a[j + 1]), chs2, pk2((j + joff == lane) ? sG : 0.f, (j + 1 + joff == lane) ? sG : 0.f));
+            else g = mul2(pk2(a[j], a[j + 1]), chs2);
+            const __half2 h = cvt_h2(g);
+            hm = __hmax2(hm, __habs2(h));
+            hp[e] = h2u(h);
+        }
+        sts128(gh_row + (((2 * j16 + q) ^ rx) << 4), hp[0], hp[1], hp[2], hp[3]);
     }
 }
 
-// Y += W * V for K steps [ks0, ks1) with W (hi at a_hi, lo at a_lo) in TMEM.
-__device__ __forceinline__ void issue_mma_ts(uint32_t acc, uint32_t a_hi, uint32_t a_lo, uint32_t b_hi,
-                                             uint32_t b_lo, int ks0, int ks1, int nterm, bool first) {
-    constexpr uint32_t idesc = (1u << 4) | (1u << 16) | ((uint32_t)(kTile >> 3) << 17) | ((uint32_t)(kTile >> 4) << 24);
-    for (int ks = ks0; ks < ks1; ++ks) {
-        mma_f16_ts(acc, a_hi + ks * 8, desc_b(b_hi, ks), idesc, (first && ks == ks0) ? 0u : 1u);
-        if (nterm == 3) {
-            mma_f16_ts(acc, a_hi + ks * 8, desc_b(b_lo, ks), idesc, 1u);
-            mma_f16_ts(acc, a_lo + ks * 8, desc_b(b_hi, ks), idesc, 1u);
+// fp16 hi (lo = false) or lo (lo = true) part of 16 values times s, packed
+// in pairs (element 2i in the low half).
+__device__ __forceinline__ void split_half(const float (&v)[16], float s, bool lo, uint32_t (&out)[8]) {
+    const uint64_t ss = pk2(s, s);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+        const uint64_t xs = mul2(pk2(v[2 * e], v[2 * e + 1]), ss);
+        __half2 hh = cvt_h2(xs);
+        if (lo) {
+            const float2 hb = __half22float2(hh);
+            hh = cvt_h2(sub2(xs, pk2(hb.x, hb.y)));
         }
+        out[e] = h2u(hh);
     }
+}
+
+// Max over the lanes of this warp that hold rows of the same matrix (the
+// rows of one matrix are consecutive lanes); bit i of `seg` is set when lane
+// + 2^i holds a row of the same matrix.  The matrix's first lane in the warp
+// ends with the warp's maximum.
+__device__ __forceinline__ float seg_max(float v, uint32_t seg) {
+#pragma unroll
+    for (int i = 0; i < 5; ++i) {
+        const float w = __shfl_down_sync(0xffffffffu, v, 1 << i);
+        if (seg & (1u << i)) v = fmaxf(v, w);
+    }
+    return v;
+}
+
+// seg_max for non-negative values; when one matrix owns all 32 rows of the
+// warp (`warp_one`) it is a single warp-wide integer max of the float bits.
+__device__ __forceinline__ float seg_max_nn(float v, uint32_t seg, bool warp_one) {
+    if (warp_one) return __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(v)));
+    return seg_max(v, seg);
+}
+
+// Order-preserving map of floats to unsigned ints (for atomicMax on signed values).
+__device__ __forceinline__ uint32_t ord_bits(float f) {
+    const uint32_t u = __float_as_uint(f);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float ord_float(uint32_t u) {
+    return __uint_as_float((u & 0x80000000u) ? (u & 0x7fffffffu) : ~u);
 }
 
 struct NsShared {
-    uint64_t bar[3];            // W columns [0,64), W columns [64,128), Y
+    uint64_t bar[2];          // [0]: H = P V complete, [1]: Y = V G complete
     uint32_t tmem_base;
-    float red[kNsThreads / 32][4];
-    float colsum[kTile];
+    uint32_t gmax[2][kTile];  // per matrix of the tile: max|G * sG| (float bits), by iteration parity
+    uint32_t vmax[2][kTile];  // per matrix: max|V| (float bits), by iteration parity
+    uint32_t stat[4][kTile];  // set-up: max signed row sum (ordered bits), max |row| sum, max |column| sum, max|P|
+    float part[2][kTile][4];  // set-up: the two column halves' row sum, |row| sum, max|P| and |column| sum
 };
 
-// One K-range of a product into the accumulator: N columns (64 or 128),
-// nterm = 1 (hi*hi) or 3 (hi*hi + hi*lo + lo*hi).  b_* may point into the
-// second 64-column block for an N = 64 product.
-template <int N>
-__device__ __forceinline__ void issue_mma(uint32_t acc, uint32_t a_hi, uint32_t a_lo, uint32_t b_hi,
-                                          uint32_t b_lo, int ks0, int ks1, int nterm, bool first) {
-    constexpr uint32_t idesc = (1u << 4) | (1u << 16) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(kTile >> 4) << 24);
-    for (int ks = ks0; ks < ks1; ++ks) {
-        mma_f16(acc, desc_a(a_hi, ks), desc_b(b_hi, ks), idesc, (first && ks == ks0) ? 0u : 1u);
-        if (nterm == 3) {
-            mma_f16(acc, desc_a(a_hi, ks), desc_b(b_lo, ks), idesc, 1u);
-            mma_f16(acc, desc_a(a_lo, ks), desc_b(b_hi, ks), idesc, 1u);
+// Set-up staging tile: 128x128 fp32, 16-byte chunk c/4 of row i at chunk
+// (c/4) ^ (i%32).  Float4 row accesses by lanes over rows or over chunks,
+// and scalar column reads by lanes over columns or rows, are conflict-free.
+__device__ __forceinline__ int stage_idx(int i, int c) { return i * kTile + ((((c >> 2) ^ i) & 31) << 2) + (c & 3); }
+__device__ __forceinline__ float4 stage_ld4(const float* st, int i, int c4) {
+    return *reinterpret_cast<const float4*>(st + i * kTile + (((c4 ^ i) & 31) << 2));
+}
+__device__ __forceinline__ void stage_st4(float* st, int i, int c4, float4 v) {
+    *reinterpret_cast<float4*>(st + i * kTile + (((c4 ^ i) & 31) << 2)) = v;
+}
+
+// Row `row`, columns [c0, c0+64) of the iterate to the output (columns of
+// the row's own matrix only).  xr points at the row's first element.
+template <typename T>
+__device__ __forceinline__ void store_rows(T* __restrict__ xr, int c0, int bn, int n, const float (&v)[64]) {
+    if constexpr (sizeof(T) == 4) {
+        if (n == kTile && (reinterpret_cast<uintptr_t>(xr + c0) & 15) == 0) {
+#pragma unroll
+            for (int j = 0; j < 64; j += 4)
+                *reinterpret_cast<float4*>(xr + c0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+            return;
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < 64; ++j) {
+        const int c = c0 + j - bn;
+        if ((unsigned)c < (unsigned)n) xr[c] = Elem<T>::store(v[j]);
+    }
+}
+
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(r[0]),
+                 "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+                 : "memory");
+}
+
+// H (+)= P V with A = P from tensor memory (hi at a_phi, lo at a_plo) and B =
+// V from shared memory (descriptors of K step 0; a K step of 16 rows is 2 KB,
+// 128 in the descriptor's address field).  FULL adds P_hi V_lo + P_lo V_hi.
+template <bool FULL>
+__device__ __forceinline__ void issue_h(uint32_t acc, uint32_t a_phi, uint32_t a_plo, uint64_t dvh, uint64_t dvl,
+                                        uint32_t go) {
+#pragma unroll
+    for (int ks = 0; ks < kTile / 16; ++ks) {
+        mma_f16_ts(acc, a_phi + ks * 8, dvh + (uint64_t)(ks * 128), kIdesc, ks > 0 ? 1u : 0u, go);
+        if (FULL) {
+            mma_f16_ts(acc, a_phi + ks * 8, dvl + (uint64_t)(ks * 128), kIdesc, 1u, go);
+            mma_f16_ts(acc, a_plo + ks * 8, dvh + (uint64_t)(ks * 128), kIdesc, 1u, go);
         }
     }
 }
 
-// Block-wide max of four values (two __syncthreads).
-__device__ __forceinline__ void block_max4(float (&v)[4], NsShared& sh) {
+// Y (+)= V G with A = V (K-major view; a K step is 32 bytes within a 64-column
+// block of 16 KB) and B = G (MN-major), both in shared memory.  FULL adds V_lo G.
+template <bool FULL>
+__device__ __forceinline__ void issue_y(uint32_t acc, uint64_t dah, uint64_t dal, uint64_t dg, uint32_t go) {
 #pragma unroll
-    for (int k = 0; k < 4; ++k)
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) v[k] = fmaxf(v[k], __shfl_xor_sync(0xffffffffu, v[k], o));
-    const int warp = threadIdx.x >> 5;
-    __syncthreads();
-    if ((threadIdx.x & 31) == 0)
-#pragma unroll
-        for (int k = 0; k < 4; ++k) sh.red[warp][k] = v[k];
-    __syncthreads();
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        float m = sh.red[0][k];
-        for (int w = 1; w < kNsThreads / 32; ++w) m = fmaxf(m, sh.red[w][k]);
-        v[k] = m;
+    for (int ks = 0; ks < kTile / 16; ++ks) {
+        const uint64_t ao = (uint64_t)((ks >> 2) * 1024 + (ks & 3) * 2);
+        mma_f16(acc, dah + ao, dg + (uint64_t)(ks * 128), kIdesc, ks > 0 ? 1u : 0u, go);
+        if (FULL) mma_f16(acc, dal + ao, dg + (uint64_t)(ks * 128), kIdesc, 1u, go);
     }
 }
 
-// Set-up staging tile: 128x128 fp32, element (i, c) at i*128 + swz(i, c).
-// The XOR keeps row writes (lanes over c) and column reads (lanes over i)
-// free of bank conflicts.
-__device__ __forceinline__ int stage_idx(int i, int c) { return i * kTile + (c ^ (i & 31) ^ ((c >> 5) & 3)); }
-
-// grid = batch, block = 512 threads (16 warps).  Warp w owns TMEM lanes
-// 32*(w%4).. (matrix rows) and the 32 columns 32*(w/4).. of the tile.
+// Newton–Schulz on tcgen05 tensor cores, in the residual form
+//     H = P V,  G = I - H,  V <- V + V G        (= 2V - V P V)
+// One CTA per 128x128 tile; for n <= 64 a tile holds floor(128/n) matrices
+// on its diagonal (products of block-diagonal matrices stay block-diagonal,
+// every scale is per matrix).  Two CTAs share an SM, so one CTA's epilogues
+// run while the other's products occupy the tensor pipe.
 //
-// Per iteration, with one thread issuing every MMA:
-//   W[:, 0:64]  = V P[:, 0:64]   -> bar[0]   (warps of column groups 0,1 convert it)
-//   W[:, 64:128]= V P[:, 64:128] -> bar[1]   (column groups 2,3), overlapping the first conversion
-//   Y  = W[:, 0:64] V[0:64, :]   issued as soon as groups 0,1 have stored their half of W,
-//      + W[:, 64:128] V[64:128,:] issued when groups 2,3 have     -> bar[2]
-//   V <- 2V - Y (all warps), new split scale from a block max.
-// W's split scale comes from the bound max|W| <= ||V||_inf * max|P| (known
-// before the product; ||V||_inf exactly for V0, then n * max|V|), so its
-// conversion needs no reduction.  A loose bound only lowers the magnitude of
-// the scaled values; fp16 keeps 11 significant bits down to 2^-14.
+// Storage per CTA: P (hi, lo fp16) as the A operand in tensor memory next to
+// the fp32 accumulator (256 columns); V hi/lo and G hi in shared memory
+// (96 KB, 128-byte swizzle, used as MN-major B and K-major A operands); the
+// exact fp32 V in registers (thread = row, 64 columns).
+// Per iteration (one elected lane of warp 0 issues the MMAs):
+//   H   = P_hi V_hi [+ P_hi V_lo + P_lo V_hi]     A from tensor memory
+//   G*sG = fp16((delta - H) sG)                   scale from max|G| <= 1 + ||P||_inf max|V|
+//   Y   = V_hi G_hi [+ V_lo G_hi]                 A and B from shared memory
+//   V  += Y;  V hi/lo with a scale from max|V'| <= max|V| (1 + n max|G|)
+// The bracketed terms run on "full" iterations (every iteration for split3,
+// the last two for mixed).  The V correction Y is scaled by |G|, which goes
+// to zero as the iteration converges, so a single fp16 G suffices; its V
+// factor needs hi + lo so that V's own rounding does not enter the residual.
+// max|G| and max|V| are reduced across the tile piggybacking on the two
+// barriers that hand the operands to the MMA thread.
 template <typename T>
-__global__ void __launch_bounds__(kNsThreads, 1)
-ns_tc_fwd_kernel(const T* __restrict__ a, T* __restrict__ x, int n, int iters, int mode, float reg,
-                 int precision, const float* __restrict__ lmk, int ld, float lscale) {
+__global__ void __launch_bounds__(kTcThreads, 2)
+ns_tc_fwd_kernel(const T* __restrict__ a, T* __restrict__ x, int batch, int n, int nb, int iters, int mode,
+                 float reg, int precision, const float* __restrict__ lmk, int ld, float lscale) {
     extern __shared__ __align__(16) unsigned char smem_raw[];  // re-aligned to 1024 below
+    // V hi at [0, 32K), V lo at [32K, 64K), G hi at [64K, 96K) of the aligned
+    // base; addresses are recomputed from the base where they are used, so
+    // no pointer has to stay live across the iteration loop.
     unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    unsigned char* Ph = base;
-    unsigned char* Pl = base + 1 * kOpBytes;
-    unsigned char* Vh = base + 2 * kOpBytes;
-    unsigned char* Vl = base + 3 * kOpBytes;
-    unsigned char* Wh = base + 4 * kOpBytes;
-    unsigned char* Wl = base + 5 * kOpBytes;
-    float* stage = reinterpret_cast<float*>(Wh);  // 128x128 fp32 during set-up (spans Wh and Wl)
-    NsShared& sh = *reinterpret_cast<NsShared*>(base + 6 * kOpBytes);
+    float* stage = reinterpret_cast<float*>(base + kOpBytes);  // set-up: 128x128 fp32 over V lo and G hi
+    float* LT = reinterpret_cast<float*>(base);                // landmark set-up: [kLtChunk][128] fp32
+    NsShared& sh = *reinterpret_cast<NsShared*>(base + 3 * kOpBytes);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int quad = warp & 3, cg = warp >> 2;
-    const int row = quad * 32 + lane;  // matrix row this thread owns in the epilogues
-    const int col0 = cg * 32;          // its 32 columns
-    const int64_t mat = blockIdx.x;
-    const T* A = a + mat * (int64_t)n * n;
-    T* X = x + mat * (int64_t)n * n;
+    const int quad = warp & 3, half = warp >> 2;
+    const int row = quad * 32 + lane;  // tile row (= TMEM lane) this thread owns
+    const int c0 = half * 64;          // its 64 columns
+    const uint32_t rbase = (uint32_t)(half * 16384 + row * 128);  // its row in a fp16 operand
+    const int rx = row & 7;
+    const int64_t m0 = (int64_t)blockIdx.x * nb;
+    const int nrows = (int)min((int64_t)nb, (int64_t)batch - m0) * n;
+    const bool valid = row < nrows;
+    const int blk = valid ? row / n : -1;  // matrix of the tile that owns this row
+    const int bn = valid ? blk * n : 0;
+    // which of the thread's two 32-column chunks holds its diagonal (warp-uniform)
+    const int dchunk = ((quad >> 1) == half) ? (quad & 1) : -1;
 
     if (tid == 0) {
-        for (int b = 0; b < 3; ++b) mbar_init(&sh.bar[b], 1);
+        mbar_init(&sh.bar[0], 1);
+        mbar_init(&sh.bar[1], 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (tid < kTile) sh.colsum[tid] = 0.f;
+    for (int e = tid; e < kTile; e += kTcThreads) {
+        sh.gmax[0][e] = sh.gmax[1][e] = sh.vmax[0][e] = sh.vmax[1][e] = 0u;
+        sh.stat[0][e] = sh.stat[1][e] = sh.stat[2][e] = sh.stat[3][e] = 0u;
+    }
     if (warp == 0) tmem_alloc(&sh.tmem_base, kTmemCols);
-    __syncthreads();
+    uint32_t seg = 0;
+#pragma unroll
+    for (int i = 0; i < 5; ++i) {
+        const int o = __shfl_down_sync(0xffffffffu, blk, 1 << i);
+        if (valid && lane + (1 << i) < 32 && o == blk) seg |= 1u << i;
+    }
+    const int prev = __shfl_up_sync(0xffffffffu, blk, 1);
+    const bool leader = valid && (lane == 0 || prev != blk);
+    // (the shuffle runs on every lane: it must not sit behind the `valid &&`)
+    const int blk0 = __shfl_sync(0xffffffffu, blk, 0);
+    const bool warp_one = __all_sync(0xffffffffu, valid && blk == blk0);
 
-    // ---- optional: A from landmarks -------------------------------------------
-    // With lmk != nullptr, A[i][c] = exp(lscale * sum_k |L[i][k] - L[c][k]|)
-    // is formed here (the channel sum in order with the LaplaceSub forward's
-    // fp32 operations, so A is bit-identical to lf_laplace_kernel_fwd(L, L^T)).
-    // L^T of this matrix is staged as LT[k][c] in the Vh/Vl region (free until
-    // V0 is written after the set-up): row i is a warp-uniform broadcast and a
-    // lane's four columns one 16-byte load.
-    float* LT = reinterpret_cast<float*>(Vh);
+    // ---- set-up: P = A + reg I into the staging tile ------------------------
     if (lmk) {
-        const float* Lb = lmk + mat * (int64_t)n * ld;
-        for (int e = tid; e < ld * kTile; e += kNsThreads) {
-            const int c = e / ld, k = e - c * ld;  // coalesced read of L[c][k]
-            LT[k * kTile + c] = (c < n) ? Lb[(int64_t)c * ld + k] : 0.f;
-        }
-        __syncthreads();
-    }
-
-    // ---- set-up: P = A + reg I into the staging tile -------------------------
-    // Warp w loads rows w, w+16, ...; lane l holds columns 4l..4l+3.
-    float mx[4] = {-1e30f, 0.f, 0.f, 0.f};  // signed row sum, |row| sum, max|P|, |col| sum
-    float colacc[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int i = warp; i < kTile; i += kNsThreads / 32) {
-        float v[4];
-        float lsum[4] = {0.f, 0.f, 0.f, 0.f};
-        if (lmk && i < n) {
-            for (int k = 0; k < ld; ++k) {
-                const float li = LT[k * kTile + i];
-                const float4 lc = *reinterpret_cast<const float4*>(LT + k * kTile + 4 * lane);
-                lsum[0] = add_abs_ftz(lsum[0], sub_ftz(li, lc.x));
-                lsum[1] = add_abs_ftz(lsum[1], sub_ftz(li, lc.y));
-                lsum[2] = add_abs_ftz(lsum[2], sub_ftz(li, lc.z));
-                lsum[3] = add_abs_ftz(lsum[3], sub_ftz(li, lc.w));
+        // A[i][c] = exp(lscale * sum_k |L[i][k] - L[c][k]|), channel sums in
+        // order with the LaplaceSub forward's fp32 operations, so A is
+        // bit-identical to lf_laplace_kernel_fwd(L, L^T).
+        float acc[64];
+#pragma unroll
+        for (int j = 0; j < 64; ++j) acc[j] = 0.f;
+        for (int k0 = 0; k0 < ld; k0 += kLtChunk) {
+            const int kc = min(kLtChunk, ld - k0);
+            __syncthreads();  // the previous chunk has been consumed
+            {
+                const int i = tid & (kTile - 1);
+                const bool iv = i < nrows;
+                const float* Lr = lmk + (iv ? ((m0 + i / n) * (int64_t)n + i % n) * ld + k0 : 0);
+                for (int kk = tid >> 7; kk < kc; kk += kTcThreads / kTile) LT[kk * kTile + i] = iv ? Lr[kk] : 0.f;
+            }
+            __syncthreads();
+            if (valid) {
+                for (int kk = 0; kk < kc; ++kk) {
+                    const float li = LT[kk * kTile + row];
+                    const float4* lc = reinterpret_cast<const float4*>(LT + kk * kTile + c0);
+#pragma unroll
+                    for (int j4 = 0; j4 < 16; ++j4) {
+                        const float4 w = lc[j4];
+                        acc[4 * j4 + 0] = add_abs_ftz(acc[4 * j4 + 0], sub_ftz(li, w.x));
+                        acc[4 * j4 + 1] = add_abs_ftz(acc[4 * j4 + 1], sub_ftz(li, w.y));
+                        acc[4 * j4 + 2] = add_abs_ftz(acc[4 * j4 + 2], sub_ftz(li, w.z));
+                        acc[4 * j4 + 3] = add_abs_ftz(acc[4 * j4 + 3], sub_ftz(li, w.w));
+                    }
+                }
             }
         }
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            int c = 4 * lane + e;
-            float t = 0.f;
-            if (i < n && c < n) {
-                const float av = lmk ? expf(lscale * lsum[e]) : Elem<T>::load(A[(int64_t)i * n + c]);
-                t = av + (i == c ? reg : 0.f);
-            }
-            v[e] = t;
-            stage[stage_idx(i, c)] = t;
-            colacc[e] += fabsf(t);
-            mx[2] = fmaxf(mx[2], fabsf(t));
-        }
-        float rs = (v[0] + v[1]) + (v[2] + v[3]);
-        float ra = (fabsf(v[0]) + fabsf(v[1])) + (fabsf(v[2]) + fabsf(v[3]));
+        for (int j4 = 0; j4 < 16; ++j4) {
+            float t[4];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            rs += __shfl_xor_sync(0xffffffffu, rs, o);
-            ra += __shfl_xor_sync(0xffffffffu, ra, o);
+            for (int q = 0; q < 4; ++q) {
+                const int c = c0 + 4 * j4 + q;
+                t[q] = 0.f;
+                if (valid && (unsigned)(c - bn) < (unsigned)n) t[q] = expf(lscale * acc[4 * j4 + q]) + (c == row ? reg : 0.f);
+            }
+            stage_st4(stage, row, (c0 >> 2) + j4, make_float4(t[0], t[1], t[2], t[3]));
         }
-        if (i < n) {
-            mx[0] = fmaxf(mx[0], rs);
-            mx[1] = fmaxf(mx[1], ra);
+    } else {
+        // Gather: warp w covers tile rows w, w+8, ...; lane l columns 4l..4l+3.
+        const T* A = a + m0 * (int64_t)n * n;
+        int b = warp / n, r = warp - (warp / n) * n;  // matrix and row within it of tile row `warp`
+#pragma unroll 4
+        for (int it = 0; it < kTile / 8; ++it) {
+            const int i = warp + 8 * it;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (i < nrows) {
+                const int ib = b * n;
+                const T* Ar = A + ((int64_t)b * n + r) * n - ib;  // Ar[c] for c in [ib, ib+n)
+                bool done = false;
+                if constexpr (sizeof(T) == 4) {
+                    if (n == kTile && (reinterpret_cast<uintptr_t>(Ar + 4 * lane) & 15) == 0) {
+                        v = *reinterpret_cast<const float4*>(Ar + 4 * lane);
+                        done = true;
+                    }
+                }
+                if (!done) {
+                    float* vp = &v.x;
+#pragma unroll
+                    for (int q = 0; q < 4; ++q)
+                        if ((unsigned)(4 * lane + q - ib) < (unsigned)n) vp[q] = Elem<T>::load(Ar[4 * lane + q]);
+                }
+                if ((i >> 2) == lane) (&v.x)[i & 3] += reg;
+            }
+            stage_st4(stage, i, lane, v);
+            r += 8;
+            while (r >= n) { r -= n; ++b; }
         }
     }
-    // column |sums|: per-warp partials combined in warp order (deterministic,
-    // so equal inputs give equal bits); Ph is free until P is split below
-    float* cpart = reinterpret_cast<float*>(Ph);  // [16 warps][kTile]
-#pragma unroll
-    for (int e = 0; e < 4; ++e) cpart[warp * kTile + 4 * lane + e] = colacc[e];
     __syncthreads();
-    if (tid < kTile) {
-        float cs = 0.f;
-        for (int w = 0; w < kNsThreads / 32; ++w) cs += cpart[w * kTile + tid];
-        mx[3] = cs;
-    }
-    block_max4(mx, sh);
-    const float pmax = mx[2];
-    const float v0_scale = (mode == LF_NS_INIT_REFERENCE) ? __fdiv_rn(1.8f, mx[0] * mx[0])
-                                                         : __fdiv_rn(1.0f, mx[3] * mx[1]);
-    const float sP = split_scale(pmax);
-    float sV = split_scale(pmax * fabsf(v0_scale));
-    // ||V0||_inf: alpha*||P||_inf, or c*||P||_1 for V0 = c P^T.
-    float vinf = fabsf(v0_scale) * (mode == LF_NS_INIT_REFERENCE ? mx[1] : mx[3]);
 
-    tc_fence_after();
-    const uint32_t tmem = sh.tmem_base;
-    const uint32_t t_lane = (uint32_t)(quad * 32) << 16;
-    const uint32_t t_w = tmem + t_lane;              // W accumulator, columns [0,128)
-    const uint32_t t_y = tmem + t_lane + kTile;      // Y accumulator, columns [128,256)
-    const uint32_t t_v = tmem + t_lane + 2 * kTile;  // fp32 V, columns [256,384)
-    const uint32_t t_wa = tmem + t_lane + 3 * kTile;  // W hi [384,448) and lo [448,512), fp16 pairs
-    const uint32_t a_whi = tmem + 3 * kTile, a_wlo = tmem + 3 * kTile + kTile / 2;  // as MMA A operands
+    // ---- per-matrix statistics (rows and columns of the tile are the
+    // thread's `row` index; the two column halves meet in shared memory) ------
     {
-        float pv[32], vv[32];
-#pragma unroll
-        for (int e = 0; e < 32; ++e) {
-            int c = col0 + e;
-            pv[e] = stage[stage_idx(row, c)];
-            float src = (mode == LF_NS_INIT_REFERENCE) ? pv[e] : stage[stage_idx(c, row)];
-            vv[e] = src * v0_scale;
+        float rs = 0.f, ra = 0.f, pm = 0.f, cs = 0.f;
+#pragma unroll 4
+        for (int c4 = 0; c4 < 16; ++c4) {
+            const float4 p = stage_ld4(stage, row, 16 * half + c4);
+            rs += (p.x + p.y) + (p.z + p.w);
+            ra += (fabsf(p.x) + fabsf(p.y)) + (fabsf(p.z) + fabsf(p.w));
+            pm = fmaxf(pm, fmaxf(fmaxf(fabsf(p.x), fabsf(p.y)), fmaxf(fabsf(p.z), fabsf(p.w))));
         }
-        split_store(Ph, Pl, row, col0, pv, sP);
-        if (iters > 0) {
-            split_store(Vh, Vl, row, col0, vv, sV);
-            tmem_st32(t_v + col0, vv);
-            tmem_wait_st();
-        } else if (row < n) {
-#pragma unroll
-            for (int e = 0; e < 32; ++e)
-                if (col0 + e < n) X[(int64_t)row * n + col0 + e] = Elem<T>::store(vv[e]);
+#pragma unroll 8
+        for (int i = 64 * half; i < 64 * half + 64; ++i) cs += fabsf(stage[stage_idx(i, row)]);
+        sh.part[half][row][0] = rs;
+        sh.part[half][row][1] = ra;
+        sh.part[half][row][2] = pm;
+        sh.part[half][row][3] = cs;
+    }
+    __syncthreads();
+    {
+        float rs = sh.part[0][row][0] + sh.part[1][row][0];
+        float ra = sh.part[0][row][1] + sh.part[1][row][1];
+        float pm = fmaxf(sh.part[0][row][2], sh.part[1][row][2]);
+        float cs = sh.part[0][row][3] + sh.part[1][row][3];
+        rs = seg_max(rs, seg);
+        ra = seg_max(ra, seg);
+        pm = seg_max(pm, seg);
+        cs = seg_max(cs, seg);
+        if (leader && half == 0) {
+            atomicMax(&sh.stat[0][blk], ord_bits(rs));
+            atomicMax(&sh.stat[1][blk], __float_as_uint(ra));
+            atomicMax(&sh.stat[2][blk], __float_as_uint(cs));
+            atomicMax(&sh.stat[3][blk], __float_as_uint(pm));
         }
     }
-    fence_async_smem();
-    tc_fence_before();
-    __syncthreads();  // staging reads done before W is overwritten; operands visible
+    __syncthreads();
 
-    const uint32_t aPh = smem_u32(Ph), aPl = smem_u32(Pl), aVh = smem_u32(Vh), aVl = smem_u32(Vl);
-    const uint32_t aWh = smem_u32(Wh), aWl = smem_u32(Wl);
-    uint32_t phase = 0;
+    // V0 = c P (reference: c = 1.8 / (max_i sum_j P_ij)^2, :82-120, :176-178)
+    // or c P^T (c = 1 / (||P||_1 ||P||_inf)).
+    float sP = 1.f, sV = 1.f, pinf = 0.f, cinit = 0.f;
+    if (valid) {
+        const float rsmax = ord_float(sh.stat[0][blk]);
+        const float ra = __uint_as_float(sh.stat[1][blk]);
+        const float ca = __uint_as_float(sh.stat[2][blk]);
+        const float pmax = __uint_as_float(sh.stat[3][blk]);
+        cinit = (mode == LF_NS_INIT_REFERENCE) ? __fdiv_rn(1.8f, rsmax * rsmax) : __fdiv_rn(1.0f, ca * ra);
+        sP = split_scale(pmax);
+        sV = split_scale(fabsf(cinit) * pmax);  // max|V0| = |c| max|P|, exactly
+        pinf = ra;
+        if (leader && half == 0) atomicMax(&sh.vmax[0][blk], __float_as_uint(fabsf(cinit) * pmax));
+    }
+    const uint32_t tmem = sh.tmem_base;
+    const uint32_t tl = (uint32_t)(quad * 32) << 16;  // this warp's TMEM lane quadrant
+    float V[64];
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+        float p[16];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const float4 w = stage_ld4(stage, row, (c0 >> 2) + 4 * g + q);
+            p[4 * q] = w.x; p[4 * q + 1] = w.y; p[4 * q + 2] = w.z; p[4 * q + 3] = w.w;
+        }
+        uint32_t pk[8];
+        split_half(p, sP, false, pk);
+        tmem_st8(tmem + tl + kTile + 32 * half + 8 * g, pk);
+        split_half(p, sP, true, pk);
+        tmem_st8(tmem + tl + kTile + 64 + 32 * half + 8 * g, pk);
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+            V[16 * g + j] = cinit * ((mode == LF_NS_INIT_REFERENCE) ? p[j] : stage[stage_idx(c0 + 16 * g + j, row)]);
+    }
+    tmem_wait_st();
     bool ok = true;
-
-    for (int it = 0; it < iters; ++it) {
-        const int nterm = (precision == LF_NS_PREC_MIXED && it < iters - 2) ? 1 : 3;
-        const bool last = (it == iters - 1);
-        const float sW = split_scale(vinf * pmax);
-        NS_TRACE(it, 0);
-        // ---- W = V P in two column halves ---------------------------------
-        if (tid == 0) {
-            tc_fence_after();
-            if (kSplitW) {
-                issue_mma<64>(tmem, aVh, aVl, aPh, aPl, 0, kTile / 16, nterm, true);
-                mma_commit(&sh.bar[0]);
-                issue_mma<64>(tmem + 64, aVh, aVl, aPh + 16384, aPl + 16384, 0, kTile / 16, nterm, true);
-                mma_commit(&sh.bar[1]);
-            } else {
-                // one N = 128 product reads each A tile once (M = 128 MMAs with
-                // both operands in shared memory are bound by its bandwidth)
-                issue_mma<128>(tmem, aVh, aVl, aPh, aPl, 0, kTile / 16, nterm, true);
-                mma_commit(&sh.bar[0]);
-                mma_commit(&sh.bar[1]);
-            }
-        }
-        NS_TRACE(it, 1);
-        const bool lo_half = cg < 2;
-        bool okw = mbar_wait(&sh.bar[lo_half ? 0 : 1], phase);
-        NS_TRACE(it, 2);
-        tc_fence_after();
-        {
-            float wv[32];
-            tmem_ld32(t_w + col0, wv);
-            tmem_wait_ld();
-            reg_fence(wv);
-            NS_TRACE(it, 12);
-            // acc = W * sV * sP; the stored operand is W * sW (all powers of two)
-            if (kWInTmem) {
-                uint32_t hp[16], lp[16];
-                split_pack(wv, sW * (1.f / sV) * (1.f / sP), hp, lp);
-                tmem_st16(t_wa + col0 / 2, hp);
-                tmem_st16(t_wa + kTile / 2 + col0 / 2, lp);
-                tmem_wait_st();
-            } else {
-                split_store(Wh, Wl, row, col0, wv, sW * (1.f / sV) * (1.f / sP));
-            }
-        }
-        NS_TRACE(it, 3);
+    if (iters == 0) {
+        if (valid) store_rows<T>(x + (m0 + blk) * (int64_t)n * n + (int64_t)(row - bn) * n, c0, bn, n, V);
+    } else {
+        tc_fence_before();
+        __syncthreads();  // staging reads done (V's buffers overlap it); P in TMEM
+        store_v(smem_u32(base) + rbase, rx, V, sV, precision == LF_NS_PREC_SPLIT3 || iters <= 2);
         fence_async_smem();
         tc_fence_before();
-        // ---- Y = W V, K split so that the first half starts early ----------
-        if (lo_half) {
-            named_sync(1, kNsThreads / 2);
-            if (tid == 0) {
-                tc_fence_after();
-                if (kWInTmem) issue_mma_ts(tmem + kTile, a_whi, a_wlo, aVh, aVl, 0, kTile / 32, nterm, true);
-                else issue_mma<128>(tmem + kTile, aWh, aWl, aVh, aVl, 0, kTile / 32, nterm, true);
-            }
+        __syncthreads();
+
+        for (int k = 0; k < iters; ++k) {
+            const uint32_t par = (uint32_t)k & 1u;
+            const bool full = precision == LF_NS_PREC_SPLIT3 || k >= iters - 2;
+            const bool last = k == iters - 1;
+            // ---- H = P V -------------------------------------------------------
             if (warp == 0) {
-                named_sync(2, kNsThreads / 2 + 32);
-                if (lane == 0) {
-                    tc_fence_after();
-                    if (kWInTmem) issue_mma_ts(tmem + kTile, a_whi, a_wlo, aVh, aVl, kTile / 32, kTile / 16, nterm, false);
-                    else issue_mma<128>(tmem + kTile, aWh, aWl, aVh, aVl, kTile / 32, kTile / 16, nterm, false);
-                    mma_commit(&sh.bar[2]);
-                }
+                tc_fence_after();
+                const uint32_t go = elect_one() ? 1u : 0u;
+                const uint32_t sb = smem_u32(base);
+                const uint64_t dvh = make_desc(sb, 16384, 1024), dvl = make_desc(sb + kOpBytes, 16384, 1024);
+                if (full) issue_h<true>(tmem, tmem + kTile, tmem + kTile + 64, dvh, dvl, go);
+                else issue_h<false>(tmem, tmem + kTile, tmem + kTile + 64, dvh, dvl, go);
+                if (go) mma_commit(&sh.bar[0]);
                 __syncwarp();
             }
-        } else {
-            named_arrive(2, kNsThreads / 2 + 32);
-        }
-        NS_TRACE(it, 4);
-        okw = mbar_wait(&sh.bar[2], phase) && okw;
-        NS_TRACE(it, 5);
-        phase ^= 1;
-        ok = !__syncthreads_or(!okw);
-        if (!ok) break;
-        tc_fence_after();
-        // ---- V <- 2V - Y ----------------------------------------------------
-        float vn[32];
-        float lmax = 0.f;
-        {
-            float yv[32];
-            tmem_ld32(t_y + col0, yv);
-            tmem_ld32(t_v + col0, vn);
-            tmem_wait_ld();
-            reg_fence(yv);
-            reg_fence(vn);
-            NS_TRACE(it, 9);
-            const float c2 = (1.f / sW) * (1.f / sV);  // acc = Y * sW * sV
-#pragma unroll
-            for (int e = 0; e < 32; ++e) {
-                vn[e] = fmaf(yv[e], -c2, 2.f * vn[e]);
-                lmax = fmaxf(lmax, fabsf(vn[e]));
+            // the other parity's reduction slots were last read before the previous barrier
+            if (tid < kTile) {
+                sh.gmax[par ^ 1u][tid] = 0u;
+                sh.vmax[par ^ 1u][tid] = 0u;
             }
-        }
-        if (last) {
-            if (row < n) {
+            const float vmk = valid ? __uint_as_float(sh.vmax[par][blk]) : 0.f;
+            const float sG = split_scale(1.f + pinf * vmk);  // |G_ij| <= 1 + ||P||_inf max|V|
+            const float chs = -sG * (1.f / sP) * (1.f / sV);
+            const uint64_t chs2 = pk2(chs, chs);
+            bool okw = mbar_wait(&sh.bar[0], par);
+            tc_fence_after();
+            // ---- G = I - H (fp16, scaled) into shared memory --------------------
+            __half2 hm = __float2half2_rn(0.f);
 #pragma unroll
-                for (int e = 0; e < 32; ++e)
-                    if (col0 + e < n) X[(int64_t)row * n + col0 + e] = Elem<T>::store(vn[e]);
+            for (int hc = 0; hc < 4; ++hc) {
+                float av[16];
+                tmem_ld16(tmem + tl + c0 + 16 * hc, av);
+                tmem_wait_ld();
+                reg_fence(av);
+                const uint32_t gh_row = smem_u32(base) + 2 * kOpBytes + rbase;
+                if ((hc >> 1) == dchunk) g_store<true>(av, chs2, sG, lane, 16 * (hc & 1), hm, gh_row, rx, hc);
+                else g_store<false>(av, chs2, sG, lane, 0, hm, gh_row, rx, hc);
             }
-            break;
-        }
-        NS_TRACE(it, 10);
-        tmem_st32(t_v + col0, vn);
+            float gm = seg_max_nn(fmaxf(__low2float(hm), __high2float(hm)), seg, warp_one);
+            if (leader) atomicMax(&sh.gmax[par][blk], __float_as_uint(gm));
+            fence_async_smem();
+            tc_fence_before();
+            if (__syncthreads_or(!okw)) { ok = false; break; }
+            // ---- Y = V G ---------------------------------------------------------
+            if (warp == 0) {
+                tc_fence_after();
+                const uint32_t go = elect_one() ? 1u : 0u;
+                const uint32_t sb = smem_u32(base);
+                const uint64_t dvh = make_desc(sb, 16, 1024), dvl = make_desc(sb + kOpBytes, 16, 1024);
+                const uint64_t dg = make_desc(sb + 2 * kOpBytes, 16384, 1024);
+                if (full) issue_y<true>(tmem, dvh, dvl, dg, go);
+                else issue_y<false>(tmem, dvh, dvl, dg, go);
+                if (go) mma_commit(&sh.bar[1]);
+                __syncwarp();
+            }
+            const float gmk = valid ? __uint_as_float(sh.gmax[par][blk]) * (1.f / sG) : 0.f;
+            // max|V + V G| <= max|V| (1 + n max|G|); the 2^-11 rounding of the
+            // fp16 maxima is far inside the factor-2 headroom of the scale
+            const float sVn = split_scale(vmk * (1.f + (float)n * gmk));
+            const uint64_t cy2 = pk2((1.f / sV) * (1.f / sG), (1.f / sV) * (1.f / sG));
+            okw = mbar_wait(&sh.bar[1], par);
+            tc_fence_after();
+            // ---- V <- V + Y ------------------------------------------------------
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) lmax = fmaxf(lmax, __shfl_xor_sync(0xffffffffu, lmax, o));
-        if (lane == 0) sh.red[warp][0] = lmax;
-        __syncthreads();
-        NS_TRACE(it, 11);
-        float m = sh.red[0][0];
-        for (int w = 1; w < kNsThreads / 32; ++w) m = fmaxf(m, sh.red[w][0]);
-        sV = split_scale(m);
-        vinf = (float)n * m;  // ||V||_inf <= n * max|V|
-        split_store(Vh, Vl, row, col0, vn, sV);
-        NS_TRACE(it, 7);
-        tmem_wait_st();
-        fence_async_smem();
-        tc_fence_before();
-        __syncthreads();
-        NS_TRACE(it, 8);
+            for (int hc = 0; hc < 4; ++hc) {
+                float av[16];
+                tmem_ld16(tmem + tl + c0 + 16 * hc, av);
+                tmem_wait_ld();
+                reg_fence(av);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const int j = 16 * hc + 2 * e;
+                    upk2(fma2(pk2(av[2 * e], av[2 * e + 1]), cy2, pk2(V[j], V[j + 1])), V[j], V[j + 1]);
+                }
+            }
+            if (last) {
+                if (!okw) ok = false;
+                else if (valid) store_rows<T>(x + (m0 + blk) * (int64_t)n * n + (int64_t)(row - bn) * n, c0, bn, n, V);
+                break;
+            }
+            float vm = store_v(smem_u32(base) + rbase, rx, V, sVn, precision == LF_NS_PREC_SPLIT3 || k + 1 >= iters - 2) *
+                       (1.f / sVn);
+            vm = seg_max_nn(vm, seg, warp_one);
+            if (leader) atomicMax(&sh.vmax[par ^ 1u][blk], __float_as_uint(vm));
+            sV = sVn;
+            fence_async_smem();
+            tc_fence_before();
+            if (__syncthreads_or(!okw)) { ok = false; break; }
+        }
     }
-    if (!ok && tid == 0) atomicExch(&g_ns_status, (int)LF_ERR_TIMEOUT);
+    if (!ok) atomicExch(&g_ns_status, (int)LF_ERR_TIMEOUT);
     tc_fence_before();
     __syncthreads();
     if (warp == 0) {
@@ -1036,21 +1163,35 @@ __global__ void bounded_wait_probe_kernel(uint64_t limit_ns) {
     if (!ok && threadIdx.x == 0) atomicExch(&g_ns_status, (int)LF_ERR_TIMEOUT);
 }
 
-size_t tc_smem_bytes() { return 6 * (size_t)kOpBytes + sizeof(NsShared) + 1024; }
+size_t tc_smem_bytes() { return 3 * (size_t)kOpBytes + sizeof(NsShared) + 1024; }
+
+// Matrices per 128x128 tile: floor(128/n) for n <= 64 (block-diagonal), else 1.
+int tc_per_tile(int64_t n) { return n <= kTile / 2 ? (int)(kTile / n) : 1; }
 
 template <typename T>
-int launch_tc_fwd(const void* a, void* x, int64_t batch, int64_t n, int iters, int mode, float reg,
-                  int precision, cudaStream_t st) {
-    size_t smem = tc_smem_bytes();
+int launch_tc(const T* a, T* x, int64_t batch, int64_t n, int iters, int mode, float reg, int precision,
+              const float* lmk, int ld, float lscale, cudaStream_t st) {
+    const size_t smem = tc_smem_bytes();
     if (smem > (size_t)max_optin_smem()) {
         set_error("NewtonInverse tensor-core path needs %zu bytes of shared memory", smem);
         return LF_ERR_UNSUPPORTED;
     }
+    const int nb = tc_per_tile(n);
+    const int64_t tiles = (batch + nb - 1) / nb;
+    if (tiles > 0x7fffffffLL) { set_error("batch too large"); return LF_ERR_UNSUPPORTED; }
     auto kern = ns_tc_fwd_kernel<T>;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    kern<<<(unsigned)batch, kNsThreads, smem, st>>>(static_cast<const T*>(a), static_cast<T*>(x), (int)n, iters,
-                                                    mode, reg, precision, nullptr, 0, 0.f);
+    cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    kern<<<(unsigned)tiles, kTcThreads, smem, st>>>(a, x, (int)batch, (int)n, nb, iters, mode, reg, precision, lmk,
+                                                    ld, lscale);
     return check_launch("ns_tc_fwd_kernel");
+}
+
+template <typename T>
+int launch_tc_fwd(const void* a, void* x, int64_t batch, int64_t n, int iters, int mode, float reg,
+                  int precision, cudaStream_t st) {
+    return launch_tc<T>(static_cast<const T*>(a), static_cast<T*>(x), batch, n, iters, mode, reg, precision,
+                        nullptr, 0, 0.f, st);
 }
 
 }  // namespace
@@ -1064,11 +1205,12 @@ extern "C" int lf_laplace_newton_inverse_fwd(const void* lmk, void* x, int64_t b
     if (batch < 0 || n < 0 || d < 0) { set_error("negative size"); return LF_ERR_INVALID; }
     if (batch == 0 || n == 0) return LF_OK;
     if (!lmk || !x) { set_error("null pointer"); return LF_ERR_INVALID; }
-    if (n > kTile || d < 1 || d * kTile * 4 > 2 * kOpBytes) {
-        set_error("lf_laplace_newton_inverse_fwd supports n <= %d and 1 <= d <= %d (got n=%lld, d=%lld)", kTile,
-                  2 * kOpBytes / (kTile * 4), (long long)n, (long long)d);
+    if (n > kTile || d < 1) {
+        set_error("lf_laplace_newton_inverse_fwd supports n <= %d and d >= 1 (got n=%lld, d=%lld)", kTile,
+                  (long long)n, (long long)d);
         return LF_ERR_UNSUPPORTED;
     }
+    if (d > 0x7fffffffLL) { set_error("d too large"); return LF_ERR_UNSUPPORTED; }
     if (init_mode != LF_NS_INIT_REFERENCE && init_mode != LF_NS_INIT_SCALED_TRANSPOSE) {
         set_error("unknown init mode %d", init_mode);
         return LF_ERR_INVALID;
@@ -1079,18 +1221,8 @@ extern "C" int lf_laplace_newton_inverse_fwd(const void* lmk, void* x, int64_t b
     }
     if (batch > 0x7fffffff) { set_error("batch too large"); return LF_ERR_UNSUPPORTED; }
     if (iters < 0) iters = 0;
-    const size_t smem = tc_smem_bytes();
-    if (smem > (size_t)max_optin_smem()) {
-        set_error("NewtonInverse tensor-core path needs %zu bytes of shared memory", smem);
-        return LF_ERR_UNSUPPORTED;
-    }
-    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    auto kern = ns_tc_fwd_kernel<float>;
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    kern<<<(unsigned)batch, kNsThreads, smem, st>>>(nullptr, static_cast<float*>(x), (int)n, iters, init_mode,
-                                                    (float)reg, precision, static_cast<const float*>(lmk), (int)d,
-                                                    (float)scale);
-    return check_launch("ns_tc_fwd_kernel");
+    return launch_tc<float>(nullptr, static_cast<float*>(x), batch, n, iters, init_mode, (float)reg, precision,
+                            static_cast<const float*>(lmk), (int)d, (float)scale, reinterpret_cast<cudaStream_t>(stream));
 }
 
 namespace lfb {
@@ -1253,8 +1385,3 @@ extern "C" int lf_device_status(int clear) {
     return v;
 }
 
-#ifdef LF_NS_TRACE
-extern "C" LF_API int lf_ns_trace_read(long long* out) {
-    return cudaMemcpyFromSymbol(out, g_ns_trace, sizeof(long long) * 16 * 32) == cudaSuccess ? 0 : 1;
-}
-#endif

@@ -12,7 +12,13 @@ the B200 module.  Output: oracle/_ref/Laplace_subtraction_cuda_ref.so (not
 committed; it travels to the GPU box with the working tree).
 
 Usage: python oracle/build_ref.py [REFERENCE_ROOT]
+
+REFERENCE_ROOT is the reference checkout: the argument, else the
+LF_REFERENCE_ROOT environment variable, else a ``reference`` directory next
+to this repository.
 """
+from __future__ import annotations
+
 import os
 import sys
 
@@ -21,9 +27,18 @@ OUT = os.path.join(HERE, "_ref")
 NAME = "Laplace_subtraction_cuda_ref"
 
 
-def build(ref_root: str = "/root/reference", verbose: bool = False) -> str:
+def default_root() -> str:
+    """The reference checkout: $LF_REFERENCE_ROOT, else ../reference beside the repository."""
+    env = os.environ.get("LF_REFERENCE_ROOT")
+    if env:
+        return env
+    return os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")
+
+
+def build(ref_root: str | None = None, verbose: bool = False) -> str:
     from torch.utils.cpp_extension import load
 
+    ref_root = ref_root or default_root()
     src = os.path.join(ref_root, "src")
     sources = [
         os.path.join(src, f)
@@ -65,4 +80,4 @@ def load_ref():
 
 
 if __name__ == "__main__":
-    print(build(sys.argv[1] if len(sys.argv) > 1 else "/root/reference", verbose=True))
+    print(build(sys.argv[1] if len(sys.argv) > 1 else None, verbose=True))

@@ -263,9 +263,21 @@ def test_against_reference_module(cuda, ref_module, dtype):
     torch.cuda.synchronize()
     assert torch.equal(s, s_ref)
     ga = ds.double().abs()
+    row, col = ga.sum(-1, keepdim=True), ga.sum(-2).unsqueeze(-2)
+    # fp16: the reference's own result is off by up to ~1.5e-2 * sum|dS|,
+    # because its split-K paths add partials with atomicAdd in half precision
+    # (LaplaceSubtraction_cuda_kernel.cu:260, :386), so the comparison with it
+    # takes 2e-2; ours is held to the north-star 1e-2 against the oracle on
+    # the same inputs below.
     tol = _bwd_tol(dtype) if dtype != torch.float16 else 2e-2
-    assert torch.all((dq.double() - dq_ref.double()).abs() <= tol * ga.sum(-1, keepdim=True) + 1e-30)
-    assert torch.all((dk.double() - dk_ref.double()).abs() <= tol * ga.sum(-2).unsqueeze(-2) + 1e-30)
+    assert torch.all((dq.double() - dq_ref.double()).abs() <= tol * row + 1e-30)
+    assert torch.all((dk.double() - dk_ref.double()).abs() <= tol * col + 1e-30)
+    if dtype == torch.float16:
+        dsf, qf, kf = (t.float().cpu().numpy() for t in (ds, q, kT))
+        oq = torch.from_numpy(np.asarray(O.laplace_bwd_query(dsf, qf, kf), dtype=np.float64)).to(cuda)
+        ok = torch.from_numpy(np.asarray(O.laplace_bwd_key(dsf, qf, kf), dtype=np.float64)).to(cuda)
+        assert torch.all((dq.double() - oq).abs() <= 1e-2 * row + 1e-30)
+        assert torch.all((dk.double() - ok).abs() <= 1e-2 * col + 1e-30)
 
 
 @pytest.mark.parametrize("shape,dtype,chunks", [

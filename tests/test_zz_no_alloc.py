@@ -10,6 +10,7 @@ import pytest
 import torch
 
 from laplacianformer_b200 import capi
+from oracle import oracle as O
 
 pytestmark = pytest.mark.gpu
 
@@ -37,7 +38,10 @@ def _call(fn, g, q, k):
 @pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16], ids=str)
 def test_noalloc_matches_existing_backward_twice(dtype):
     L = capi.lib()
-    shapes = [(4, 2, 3136, 32, 49), (8, 40, 64, 32, 49)]
+    # Both shapes spread each (b,h) over several CTAs, so both calls write and
+    # read scratch slots; the second differs in (b,h) count, length, landmark
+    # count and seed, so a slot left stale by the first call would change dK.
+    shapes = [(4, 2, 3136, 32, 49), (3, 1, 2000, 32, 40)]
     for call, (shape, seed) in enumerate(zip(shapes, (11, 12))):
         g, q, k = _inputs(shape, dtype, seed)
         assert 0 < L.lf_laplace_sub_bwd_workspace_size(q.shape[0] * q.shape[1], q.shape[2], k.shape[3],
@@ -52,6 +56,12 @@ def test_noalloc_matches_existing_backward_twice(dtype):
         col = ga.sum(-2).unsqueeze(-2)
         assert torch.all((dq.double() - rq.double()).abs() <= TOL[dtype] * row), f"dQ, call {call + 1}"
         assert torch.all((dk.double() - rk.double()).abs() <= TOL[dtype] * col), f"dK, call {call + 1}"
+        # and against the CPU oracle of the reference arithmetic, on the same inputs
+        gf, qf, kf = (t.float().cpu().numpy() for t in (g, q, k))
+        oq = torch.from_numpy(np.asarray(O.laplace_bwd_query(gf, qf, kf), dtype=np.float64))
+        ok = torch.from_numpy(np.asarray(O.laplace_bwd_key(gf, qf, kf), dtype=np.float64))
+        assert torch.all((dq.double().cpu() - oq).abs() <= TOL[dtype] * row.cpu()), f"dQ vs oracle, call {call + 1}"
+        assert torch.all((dk.double().cpu() - ok).abs() <= TOL[dtype] * col.cpu()), f"dK vs oracle, call {call + 1}"
 
 
 def test_noalloc_rejects_shapes_beyond_its_scratch():
