@@ -1,17 +1,31 @@
 """Benchmark: LaplaceSubtraction forward+backward (Gdist/s) on the pyramid-ViT
-stage-1 shape, with the batched NewtonInverse (matrices/s) reported beside it.
+stage-1 shape, with the batched NewtonInverse (matrices/s), the long-sequence
+configuration 5 and the configuration-4 attention block reported beside it.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 
-One process per GPU (torchrun for N > 1).  The path shards over B*H with no
-collective: every rank runs its own batch-32 slice of a global batch 32*N
-(weak scaling).  A step is one pass of the hot path over one batch: S =
+One process per GPU (torchrun for N > 1).  The headline path shards over B*H
+with no collective: every rank runs its own batch-32 slice of a global batch
+32*N (weak scaling).  A step is one pass of the hot path over one batch: S =
 LaplaceSub(Q, K^T), then both gradients (dQ, dK^T) of an upstream dS, through
 the C ABI with inputs resident in HBM.  Timing: W untimed steps, then K steps
 bracketed by a barrier and cudaDeviceSynchronize; each step is timed with CUDA
 events on the launching stream and an L2 flush (a 256 MB write, outside the
-events) separates steps; the max over ranks is reported.  rank 0 prints one
-JSON line.
+events) separates steps; a GPU sleep enqueued ahead of the timed steps lets
+the host queue them all, so host launch jitter never shows up as device time;
+the max over ranks is reported, and the per-rank figures are listed.  Rank 0
+prints one JSON line.
+
+Sub-records of the same line:
+* ``newton_inverse`` — configuration 3 (4096 x 128^2, 12 iterations) with
+  the scaled-transpose init in split3 and mixed arithmetic, and the drop-in
+  NewtonInverse_forward (reference init, A + 0.01 I, split3);
+* ``config5`` — the north-star long-sequence workload (B=8, H=16, N=16384,
+  D=64, M=256, bf16 LaplaceSub fwd+bwd + the 256x256 landmark inverse x10)
+  strong-scaled over the ranks, with dQ, dK^T and X all-gathered over NCCL
+  after the compute when N > 1;
+* ``config4`` — the Laplacian attention block fwd+bwd, bf16 [128,8,196,64],
+  M = 49, 8 iterations (rank 0 of a 1-GPU run).
 
 --impl reference times the reference's own operators (compiled from its
 sources for sm_100 into oracle/_ref by oracle/build_ref.py) on the same
@@ -99,14 +113,19 @@ def _flush_buffer(dev):
     return torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
 
 
-def time_steps(step, steps, warmup, flush, stream, kernel_events=None):
-    """Warm up, then time `steps` calls of step() with events on `stream`."""
+def time_steps(step, steps, warmup, flush, stream, prefill_ms=5.0):
+    """Warm up, then time `steps` calls of step() with events on `stream`.
+
+    A GPU sleep of `prefill_ms` is enqueued before the timed steps so that the
+    host has queued them all before the GPU reaches them (outside the events)."""
     for _ in range(warmup):
         step()
     torch.cuda.synchronize()
     if torch.distributed.is_initialized():
         torch.distributed.barrier()
     torch.cuda.synchronize()
+    if prefill_ms > 0:
+        torch.cuda._sleep(int(prefill_ms * 2.0e6))  # ~2 GHz SM clock
     evs = []
     for _ in range(steps):
         flush.zero_()
@@ -120,6 +139,17 @@ def time_steps(step, steps, warmup, flush, stream, kernel_events=None):
     if torch.distributed.is_initialized():
         torch.distributed.barrier()
     return [a.elapsed_time(b) for a, b in evs]
+
+
+def per_rank(values):
+    """All ranks' values of a few floats (list per rank); [values] on one process."""
+    if not torch.distributed.is_initialized():
+        return [list(values)]
+    world = torch.distributed.get_world_size()
+    t = torch.tensor(list(values), dtype=torch.float64, device=torch.device("cuda", torch.cuda.current_device()))
+    out = [torch.empty_like(t) for _ in range(world)]
+    torch.distributed.all_gather(out, t)
+    return [[round(float(x), 5) for x in o.tolist()] for o in out]
 
 
 def max_over_ranks(x: float) -> float:
@@ -168,9 +198,43 @@ def cpu_baseline_laplace(w, threads):
                       f"{el:.1f} s on {O.threads()} host threads, oracle/oracle.c"}
 
 
-def newton_section(dev, steps, warmup, flush, stream, peaks, peak_kind, quick=False):
-    """Configuration 3: 4096 SPD 128x128 matrices, 12 iterations, fp32,
-    scaled-transpose init; matrices/s and the tensor-pipe roofline."""
+def cpu_baseline_eager(w, threads, budget_s=8.0):
+    """The reference semantics in PyTorch eager on the host cores (the form the
+    north star names): S = cdist_1(Q, L), dQ = sum_j dS sign(Q - L_j), dK^T =
+    -sum_i dS sign(Q_i - L), over a bounded sample of (b,h) slices."""
+    torch.set_num_threads(threads)
+    q = w["q"].cpu().float()
+    kT = w["kT"].cpu().float()
+    g = w["ds"].cpu().float()
+    B, H, N, D = q.shape
+    M = kT.shape[-1]
+    done = 0
+    t0 = time.perf_counter()
+    for b in range(B):
+        for h in range(H):
+            qs, L, gs = q[b, h], kT[b, h].t().contiguous(), g[b, h]
+            torch.cdist(qs[None], L[None], p=1)
+            for r0 in range(0, N, 512):  # bounded intermediate [512, M, D]
+                sg = torch.sign(qs[r0:r0 + 512, None, :] - L[None, :, :])
+                gr = gs[r0:r0 + 512, :, None]
+                (gr * sg).sum(1)
+                (gr * sg).sum(0)
+            done += 1
+            if time.perf_counter() - t0 > budget_s:
+                break
+        if time.perf_counter() - t0 > budget_s:
+            break
+    el = time.perf_counter() - t0
+    return {"value": done * N * M / el / 1e9, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{done} of {B * H} (b,h) slices, PyTorch eager fp32 on the host (cdist p=1 + sign sums), "
+                      f"{el:.1f} s"}
+
+
+def newton_section(dev, steps, warmup, flush, stream, peaks, peak_kind):
+    """Configuration 3: 4096 SPD 128x128 matrices, 12 iterations, fp32:
+    scaled-transpose init in split3 and mixed arithmetic, and the drop-in
+    NewtonInverse_forward (reference init, A + 0.01 I, split3) that the
+    reference arm times; matrices/s and the tensor-pipe roofline."""
     from laplacianformer_b200 import capi, workloads
 
     batch = 4096
@@ -178,26 +242,66 @@ def newton_section(dev, steps, warmup, flush, stream, peaks, peak_kind, quick=Fa
     A, iters = w["A"], w["iters"]
     X = torch.empty_like(A)
     out = {}
-    for name, prec in (("split3", capi.PREC_SPLIT3), ("mixed", capi.PREC_MIXED)):
+    flops = batch * iters * 4.0 * 128 ** 3
+    # products issued per iteration, in units of one 128^3 product: H = P V
+    # (3 terms on full iterations) and Y = V G (2 terms on full iterations)
+    runs = (("split3", capi.INIT_SCALED_TRANSPOSE, 0.0, capi.PREC_SPLIT3, 5.0),
+            ("mixed", capi.INIT_SCALED_TRANSPOSE, 0.0, capi.PREC_MIXED, (5.0 * 2 + 2.0 * (iters - 2)) / iters),
+            ("dropin", capi.INIT_REFERENCE, 0.01, capi.PREC_SPLIT3, 5.0))
+    for name, init, reg, prec, units in runs:
         def step():
-            capi.newton_inverse_fwd(A, iters, init_mode=capi.INIT_SCALED_TRANSPOSE, precision=prec, out=X)
+            capi.newton_inverse_fwd(A, iters, init_mode=init, reg=reg, precision=prec, out=X)
         times = time_steps(step, max(2, steps // 2), max(3, warmup), flush, stream)
         ms = max_over_ranks(statistics.mean(times))
-        res = capi.newton_inverse_residual(A, X, 0.0)
-        flops = batch * iters * 4.0 * 128 ** 3
-        nmma = 3 if prec == capi.PREC_SPLIT3 else (3 * 2 + 1 * (iters - 2)) / iters
+        res = capi.newton_inverse_residual(A, X, reg)
+        ach = flops / (ms / 1e3) / 1e12
         out[name] = {
             "value": batch / (ms / 1e3), "unit": "matrices/s", "ms_per_step": ms,
+            "init": "reference (A + 0.01 I, alpha = 1.8/rowsum^2), the drop-in NewtonInverse_forward"
+                    if name == "dropin" else "scaled transpose (A^T / (||A||_1 ||A||_inf))",
             "residual_fro_max": float(res.max().item()), "residual_fro_mean": float(res.mean().item()),
-            "roofline": {"bound": "tensor", "achieved": flops / (ms / 1e3) / 1e12,
-                         "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-                         "frac": flops / (ms / 1e3) / 1e12 / peaks["bf16_tflops"],
+            "roofline": {"bound": "tensor", "kernel": "ns_tc_fwd_kernel", "achieved": ach,
+                         "peak": peaks["bf16_tflops"], "unit": "TFLOP/s", "frac": ach / peaks["bf16_tflops"],
                          "peak_kind": f"bf16 dense burst, {peak_kind} (kind::f16 MMAs run at the same rate)",
                          "algorithmic": "4*N^3 per matrix per iteration",
-                         "issued_tensor_tflops": nmma * flops / (ms / 1e3) / 1e12,
+                         "issued_products_per_iteration": units,
+                         "issued_tensor_tflops": units / 2.0 * ach,
+                         "issued_frac": units / 2.0 * ach / peaks["bf16_tflops"],
                          "traffic": None},
         }
     return out
+
+
+# DRAM bytes of one launch of each configuration-2 fp32 kernel, from the ncu
+# capture summarised in profiles/laplace_sub_config2_fp32.md
+# (dram__bytes_read.sum + dram__bytes_write.sum).
+NCU_TRAFFIC = {"lsub_bwd_fast_kernel": 65.5e6 + 5.2e6, "lsub_fwd_kernel": 26.1e6 + 0.29e6}
+
+
+def copy_bound_ms(hin, din, hout, dout, steps, dev):
+    """Host<->device copies of one step alone: the inputs H2D on one stream and
+    the outputs D2H on another (PCIe is full duplex), as the pipeline overlaps
+    them; mean ms over `steps`."""
+    s1, s2 = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    times = []
+    for it in range(steps + 2):
+        torch.cuda.synchronize()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(s1)
+        s2.wait_event(a)
+        with torch.cuda.stream(s1):
+            for h, d in zip(hin, din):
+                d.copy_(h, non_blocking=True)
+        with torch.cuda.stream(s2):
+            for h, d in zip(hout, dout):
+                h.copy_(d, non_blocking=True)
+        s1.wait_stream(s2)
+        b.record(s1)
+        torch.cuda.synchronize()
+        if it >= 2:
+            times.append(a.elapsed_time(b))
+    return statistics.mean(times)
 
 
 def run_b200(args, rank, world, dev):
@@ -238,11 +342,13 @@ def run_b200(args, rank, world, dev):
     torch.cuda.synchronize()
     timed_f = ev_f[-args.steps:]
     timed_b = ev_b[-args.steps:]
-    fwd_ms = statistics.mean(a.elapsed_time(b) for a, b in timed_f)
-    bwd_ms = statistics.mean(a.elapsed_time(b) for a, b in timed_b)
-    ms = max_over_ranks(statistics.mean(times))
-    fwd_ms = max_over_ranks(fwd_ms)
-    bwd_ms = max_over_ranks(bwd_ms)
+    fwd_ms_r = statistics.mean(a.elapsed_time(b) for a, b in timed_f)
+    bwd_ms_r = statistics.mean(a.elapsed_time(b) for a, b in timed_b)
+    ms_r = statistics.mean(times)
+    ranks = per_rank([ms_r, fwd_ms_r, bwd_ms_r])
+    ms = max(r[0] for r in ranks)
+    fwd_ms = max(r[1] for r in ranks)
+    bwd_ms = max(r[2] for r in ranks)
     dists = bh * N * M  # per rank per step
     value = world * dists / (ms / 1e3) / 1e9
 
@@ -251,22 +357,25 @@ def run_b200(args, rank, world, dev):
     terms = bh * N * M * D
     sm_count = torch.cuda.get_device_properties(dev).multi_processor_count
     clock_mhz = clk.summary()["sm_mhz"] or peaks.get("sm_max_mhz", 1965.0)
-    issue_peak = sm_count * 4 * 32 * clock_mhz * 1e6  # thread-instructions/s at the sampled clock
+    issue_peak = sm_count * 4 * 32 * clock_mhz * 1e6  # FP32 lane-operations/s at the sampled clock
+    bwd_ops = 4 * terms  # sub, step (fma.sat), two fma per term; packed f32x2 forms count as 2
     roofline = {
-        "bound": "hbm", "kernel": "lsub_bwd_fast_kernel balanced (fused dQ + dK^T) + lsub_bwd_dk_finalize",
-        "achieved": bb / (bwd_ms / 1e3) / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-        "frac": bb / (bwd_ms / 1e3) / 1e9 / peaks["hbm_gbs"], "traffic": None,
-        "peak_kind": peak_kind,
+        "bound": "fp32_issue", "kernel": "lsub_bwd_fast_kernel balanced (fused dQ + dK^T) + lsub_bwd_dk_finalize",
+        "achieved": bwd_ops / (bwd_ms / 1e3) / 1e12, "peak": issue_peak / 1e12, "unit": "T FP32 lane-ops/s",
+        "frac": bwd_ops / (bwd_ms / 1e3) / issue_peak,
+        "peak_kind": f"{sm_count} SMs x 128 FP32 lanes x {clock_mhz:.0f} MHz (median SM clock sampled in the timed region)",
+        "algorithmic_ops_per_launch": bwd_ops,
+        "ops_per_term": "4 FP32 lane-operations (sub, fma.sat step, 2 fma); the kernel issues them as 2.5 instructions "
+                        "per term with packed f32x2 forms, each of which occupies the FP32 pipe for 2 lane-operations",
+        "traffic": NCU_TRAFFIC["lsub_bwd_fast_kernel"] if dtype == torch.float32 else None,
         "algorithmic_bytes_per_launch": bb,
-        "note": "the kernel is bounded by the FP32 issue rate, not HBM; see 'issue'",
-        "issue": {
-            "instr_per_term": 4, "achieved_tinstr_s": 4 * terms / (bwd_ms / 1e3) / 1e12,
-            "peak_tinstr_s": issue_peak / 1e12,
-            "frac": 4 * terms / (bwd_ms / 1e3) / issue_peak,
-            "peak_basis": f"{sm_count} SMs x 128 lanes x {clock_mhz:.0f} MHz (median sampled SM clock)",
-        },
-        "fwd": {"ms": fwd_ms, "achieved_gbs": fb / (fwd_ms / 1e3) / 1e9,
-                "issue_frac": 2 * terms / (fwd_ms / 1e3) / issue_peak},
+        "hbm": {"achieved_gbs": bb / (bwd_ms / 1e3) / 1e9, "peak_gbs": peaks["hbm_gbs"],
+                "frac": bb / (bwd_ms / 1e3) / 1e9 / peaks["hbm_gbs"], "peak_kind": peak_kind},
+        "fwd": {"ms": fwd_ms, "kernel": "lsub_fwd_kernel", "ops_per_term": 2,
+                "frac": 2 * terms / (fwd_ms / 1e3) / issue_peak,
+                "hbm_gbs": fb / (fwd_ms / 1e3) / 1e9,
+                "traffic": NCU_TRAFFIC["lsub_fwd_kernel"] if dtype == torch.float32 else None},
+        "step_frac": 6 * terms / (ms / 1e3) / issue_peak,
     }
 
     # End to end through the public API: pinned host buffers in, results out.
@@ -286,6 +395,7 @@ def run_b200(args, rank, world, dev):
 
     e2e_times = time_steps(e2e_step, args.steps, args.warmup, flush, stream)
     e2e_ms = max_over_ranks(statistics.mean(e2e_times))
+    copy_ms = max_over_ranks(copy_bound_ms((hq, hk, hg), (q, kT, ds), (hs, hdq, hdk), (s, dq, dk), 5, dev))
     h2d = (q.numel() + kT.numel() + ds.numel()) * es
     d2h = (s.numel() + dq.numel() + dk.numel()) * es
 
@@ -300,31 +410,45 @@ def run_b200(args, rank, world, dev):
                    "parallelism": f"bh-shard x{world}, no collective",
                    "l2": "flushed between timed steps (256 MB write outside the events)"},
         "fwd_ms": fwd_ms, "bwd_ms": bwd_ms,
+        "per_rank": {"fields": ["step_ms", "fwd_ms", "bwd_ms"], "values": ranks},
         "roofline": roofline,
         "e2e": {"value": world * dists / (e2e_ms / 1e3) / 1e9, "unit": UNIT, "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "api": "laplacianformer_b200.streaming.HostPipeline (C ABI, 8 B*H chunks on copy-in / kernel / copy-out streams) with pinned host buffers"},
+                "copy_bound_ms": copy_ms, "frac_of_copy_bound": copy_ms / e2e_ms,
+                "api": "laplacianformer_b200.streaming.HostPipeline (C ABI, 8 B*H chunks on copy-in / kernel / "
+                       "copy-out streams) with pinned host buffers; copy_bound_ms = the same copies alone, both "
+                       "PCIe directions overlapped"},
         "gpu_launches": (3 if ws is not None else 2) * args.steps,
         "clocks": clk.summary(),
     }
     if not args.skip_newton:
         line["newton_inverse"] = newton_section(dev, args.steps, args.warmup, flush, stream, peaks, peak_kind)
-        line["gpu_launches"] += sum(max(2, args.steps // 2) for _ in range(2))
+        line["gpu_launches"] += 3 * max(2, args.steps // 2)
+    if not args.skip_config5:
+        c5 = config5_record(args, rank, world, dev, args.n_tokens, "after" if world > 1 else "none", flush)
+        line["config5"] = c5
+        line["gpu_launches"] += c5.pop("launches")
+    if world == 1 and not args.skip_config4:
+        c4 = config4_record(args, dev, flush, stream)
+        line["config4"] = c4
+        line["gpu_launches"] += c4.pop("launches")
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline_laplace({"q": q, "kT": kT, "ds": ds}, os.cpu_count() or 1)
+        line["cpu_baseline_eager"] = cpu_baseline_eager({"q": q, "kT": kT, "ds": ds}, os.cpu_count() or 1)
     return line
 
 
-def run_config5(args, rank, world, dev):
+def config5_record(args, rank, world, dev, n_tokens, gather, flush):
     """Configuration 5: B=8, H=16, D=64, M=256 chunk-mean landmarks, bf16 Q/K,
     LaplaceSub fwd+bwd plus the 256x256 landmark-kernel inverse (fp32, 10
-    iterations).  Strong scaling: the 128 (b,h) slices are split over ranks."""
+    iterations).  Strong scaling: the 128 (b,h) slices are split over ranks;
+    with gather "after", dQ, dK^T and X are all-gathered over NCCL after the
+    compute (S stays sharded), and the gather is timed on its own as well."""
     from laplacianformer_b200 import capi, workloads
     from laplacianformer_b200.sharding import shard_bounds
 
     stream = torch.cuda.current_stream(dev)
-    flush = _flush_buffer(dev)
-    B, H, D, M, N = 8, 16, 64, 256, args.n_tokens
+    B, H, D, M, N = 8, 16, 64, 256, n_tokens
     lo, hi = shard_bounds(B * H, world, rank)
     bh = hi - lo
     g = torch.Generator(device=dev)
@@ -334,6 +458,7 @@ def run_config5(args, rank, world, dev):
     L = workloads.chunk_mean_landmarks(k, M)
     kT = L.transpose(-1, -2).contiguous()
     ds = torch.randn(1, bh, N, M, generator=g, device=dev).to(torch.bfloat16)
+    del k
     s = torch.empty(1, bh, N, M, device=dev, dtype=torch.bfloat16)
     dq, dk = torch.empty_like(q), torch.empty_like(kT)
     Lf = L.float().contiguous()
@@ -341,63 +466,94 @@ def run_config5(args, rank, world, dev):
     sll = torch.empty(1, bh, M, M, device=dev)
     X = torch.empty_like(sll)
     sigma = math.sqrt(D)
-
-    gather = args.gather if world > 1 else "none"
+    chunk = -(-(B * H) // world)
     gbufs = None
-    if gather != "none":
+    if gather == "after":
         # replicated dQ, dK^T and X on every rank (S stays sharded: gathering
         # it would move more bytes over NVLink than the sharded compute saves)
-        gbufs = [torch.empty((world,) + tuple(t.shape), device=dev, dtype=t.dtype) for t in (dq, dk, X)]
-    pieces = 4 if gather == "overlap" else 1
-    per = -(-bh // pieces)
-    bounds = [(i * per, min(bh, (i + 1) * per)) for i in range(pieces)]
-    pbufs = []
-    if gather == "overlap":  # one receive buffer per piece and output
-        pbufs = [[torch.empty((world, b - a) + tuple(t.shape[2:]), device=dev, dtype=t.dtype) for t in (dq, dk, X)]
-                 for a, b in bounds]
+        gbufs = [torch.empty((world * chunk,) + tuple(t.shape[2:]), device=dev, dtype=t.dtype) for t in (dq, dk, X)]
+        sends = [t[0] if bh == chunk else torch.zeros((chunk,) + tuple(t.shape[2:]), device=dev, dtype=t.dtype)
+                 for t in (dq, dk, X)]
 
-    def distances(a, b):
-        sl = slice(a, b)
-        capi.laplace_sub_fwd(q[:, sl], kT[:, sl], s[:, sl])
-        capi.laplace_sub_bwd(ds[:, sl], q[:, sl], kT[:, sl], dq[:, sl], dk[:, sl])
-
-    def inverse():
+    def compute():
+        capi.laplace_sub_fwd(q, kT, s)
+        capi.laplace_sub_bwd(ds, q, kT, dq, dk)
         capi.laplace_sub_fwd(Lf, LfT, sll)
         A = torch.exp(sll * (-1.0 / sigma))
         capi.newton_inverse_fwd(A, 10, out=X)
 
-    def step():
-        if gather == "none":
-            distances(0, bh)
-            inverse()
-            return
-        works = []
-        for i, (a, b) in enumerate(bounds):
-            distances(a, b)
-            if gather == "overlap":  # piece i's dQ/dK^T cross NVLink while piece i+1 (and the inverse) compute
-                for t, buf in zip((dq, dk), pbufs[i][:2]):
-                    works.append(torch.distributed.all_gather_into_tensor(buf, t[0, a:b], async_op=True))
-        inverse()
-        if gather == "overlap":
-            works.append(torch.distributed.all_gather_into_tensor(gbufs[2], X, async_op=True))
-        if gather == "after":
-            for t, buf in zip((dq, dk, X), gbufs):
-                torch.distributed.all_gather_into_tensor(buf, t)
-        for w in works:
-            w.wait()
+    def gather_all():
+        for i, (t, buf) in enumerate(zip((dq, dk, X), gbufs)):
+            if bh != chunk:
+                sends[i][:bh].copy_(t[0])
+            torch.distributed.all_gather_into_tensor(buf, sends[i] if bh != chunk else t[0])
 
-    times = time_steps(step, args.steps, args.warmup, flush, stream)
-    ms = max_over_ranks(statistics.mean(times))
+    def step():
+        compute()
+        if gbufs is not None:
+            gather_all()
+
+    steps = max(3, min(args.steps, 10))
+    times = time_steps(step, steps, max(3, args.warmup), flush, stream)
+    g_ms = 0.0
+    if gbufs is not None:
+        g_ms = statistics.mean(time_steps(gather_all, steps, 3, flush, stream))
+    ranks = per_rank([statistics.mean(times), g_ms])
+    ms = max(r[0] for r in ranks)
+    launches = steps * (5 + (0 if gbufs is None else 3))  # our 4 kernels + the exp; NCCL gathers are NCCL's
     return {
-        "metric": METRIC, "value": B * H * N * M / (ms / 1e3) / 1e9, "unit": UNIT, "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "value": B * H * N * M / (ms / 1e3) / 1e9, "unit": UNIT, "ms_per_step": ms, "steps": steps,
+        "gather_ms": max(r[1] for r in ranks), "scaling": "strong", "dtype": "bf16 (inverse fp32)",
+        "workload": f"config5 N={N}: LaplaceSub fwd+bwd bf16 (B*H=128, M=256, D=64) + NewtonInverse 256x256 fp32 x10",
+        "parallelism": f"bh-shard x{world} (strong), " + ("no collective" if gbufs is None else
+                                                          "dQ/dK^T/X all_gather_into_tensor over NCCL after the compute"),
+        "newton_matrices_per_s": B * H / (ms / 1e3),
+        "per_rank": {"fields": ["step_ms", "gather_ms"], "values": ranks},
+        "l2": "inputs larger than L2" if N >= 16384 else "flushed between timed steps",
+        "launches": launches,
+    }
+
+
+def config4_record(args, dev, flush, stream):
+    """Configuration 4: the Laplacian attention block forward + backward, bf16
+    Q/K/V [128,8,196,64], 49 landmarks from 2x2 pooling of K, 8 iterations."""
+    from laplacianformer_b200 import workloads
+    from laplacianformer_b200.attention import laplacian_attention
+
+    w = workloads.config4(device=dev, batch=128)
+    q, k, v = (w[x].detach().requires_grad_() for x in ("q", "k", "v"))
+    up = torch.randn_like(q)
+
+    def step():
+        L = w["landmarks"]
+        out = laplacian_attention(q, k, v, L, iters=8, sigma=8.0)
+        out.backward(up)
+
+    steps = max(3, min(args.steps, 10))
+    times = time_steps(step, steps, max(3, args.warmup), flush, stream)
+    ms = statistics.mean(times)
+    tokens = 128 * 196
+    return {"value": tokens / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms, "steps": steps,
+            "workload": "config4 Laplacian attention block fwd+bwd: Q,K,V [128,8,196,64] bf16, M=49 (2x2 pooling "
+                        "of K), sigma=8, NewtonInverse 8 iterations; landmark inverse fused (A built in-kernel)",
+            "launches": steps * 9}
+
+
+def run_config5(args, rank, world, dev):
+    """--workload config5: the configuration-5 record as the line itself."""
+    flush = _flush_buffer(dev)
+    with ClockSampler(dev.index) as clk:
+        rec = config5_record(args, rank, world, dev, args.n_tokens, args.gather if world > 1 else "none", flush)
+    launches = rec.pop("launches")
+    return {
+        "metric": METRIC, "value": rec["value"], "unit": UNIT, "n_gpus": world, "steps": rec["steps"],
+        "warmup": max(3, args.warmup), "ms_per_step": rec["ms_per_step"], "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded N(0,1), configuration-5 shapes)",
-        "config": {"workload": f"config5 N={N}: LaplaceSub fwd+bwd bf16 (M=256, D=64) + NewtonInverse 256x256 fp32 x10",
-                   "global_batch": B, "heads": H, "seq_len": N, "parallelism": f"bh-shard x{world} (strong), " + ("no collective" if gather == "none" else
-                                   f"dQ/dK/X all-gathered ({gather})"),
-                   "l2": "inputs larger than L2" if N >= 16384 else "flushed between timed steps"},
-        "newton_matrices_per_s": B * H / (ms / 1e3),
+        "config": {"workload": rec["workload"], "global_batch": 8, "heads": 16, "seq_len": args.n_tokens,
+                   "parallelism": rec["parallelism"], "l2": rec["l2"]},
+        "gather_ms": rec["gather_ms"], "per_rank": rec["per_rank"],
+        "newton_matrices_per_s": rec["newton_matrices_per_s"], "gpu_launches": launches, "clocks": clk.summary(),
     }
 
 
@@ -526,8 +682,10 @@ def main():
     ap.add_argument("--ns-batch", type=int, default=4096)
     ap.add_argument("--workload", choices=["config2", "config5"], default="config2")
     ap.add_argument("--n-tokens", type=int, default=16384, help="configuration-5 sequence length")
-    ap.add_argument("--gather", choices=["none", "after", "overlap"], default="none",
-                    help="configuration 5 with N>1: all-gather dQ, dK^T and X after the compute or overlapped per piece")
+    ap.add_argument("--gather", choices=["none", "after"], default="after",
+                    help="--workload config5 with N>1: all-gather dQ, dK^T and X after the compute (or not at all)")
+    ap.add_argument("--skip-config5", action="store_true", help="leave the configuration-5 sub-record out")
+    ap.add_argument("--skip-config4", action="store_true", help="leave the configuration-4 sub-record out")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
