@@ -50,6 +50,9 @@ constexpr int kOpBytes = kTile * kTile * 2; // one fp16 operand (32 KB)
 constexpr int kTmemCols = 256;             // accumulator [0,128), P hi [128,192), P lo [192,256)
 constexpr int kLtChunk = 64;               // landmark channels staged per set-up pass
 
+// Matrices per 128x128 tile: floor(128/n) for n <= 64 (block-diagonal), else 1.
+int tc_per_tile(int64_t n) { return n <= kTile / 2 ? (int)(kTile / n) : 1; }
+
 // ---------------------------------------------------------------------------
 // PTX wrappers (tcgen05, mbarrier, fences)
 // ---------------------------------------------------------------------------
@@ -915,6 +918,603 @@ ns_residual_kernel(const T* __restrict__ a, const T* __restrict__ x, Acc* __rest
 }
 
 // ---------------------------------------------------------------------------
+// Backward on tcgen05: dA = -(V^T G) V^T (reference :469-573), n <= 128.
+// One CTA per 128x128 tile (floor(128/n) matrices on the diagonal for
+// n <= 64).  V and G are split as hi + lo fp16 with per-matrix scales and
+// stored row-major with the 128-byte swizzle; the transposes come from the
+// descriptor views of the same bytes:
+//   T1 = V^T G   A = V as an MN-major operand (A[m][k] = V[k][m]), B = G MN-major
+//   dA = -T1 V^T A = T1 from tensor memory (hi/lo fp16), B = V as a K-major
+//                operand (B[k][n] = V[n][k])
+// each as hi*hi + hi*lo + lo*hi (the split3 arithmetic of the forward).
+// ---------------------------------------------------------------------------
+constexpr uint32_t kIdescT1 = (1u << 4) | (1u << 15) | (1u << 16) | ((uint32_t)(kTile >> 3) << 17) |
+                              ((uint32_t)(kTile >> 4) << 24);  // A and B MN-major
+constexpr uint32_t kIdescDA = (1u << 4) | ((uint32_t)(kTile >> 3) << 17) | ((uint32_t)(kTile >> 4) << 24);  // B K-major
+
+struct NsBwdShared {
+    uint64_t bar[2];
+    uint32_t tmem_base;
+    uint32_t vmax[kTile], gmax[kTile], tmax[kTile];  // per matrix of the tile (float bits)
+};
+
+// Row `row`, 64 columns of the matrix at src (rows of the tile's matrices,
+// zero outside the row's own matrix) into v.
+template <typename T>
+__device__ __forceinline__ void load_rows(const T* __restrict__ src, int64_t m0, int n, bool valid, int blk, int bn,
+                                          int row, int c0, float (&v)[64]) {
+#pragma unroll
+    for (int j = 0; j < 64; ++j) v[j] = 0.f;
+    if (!valid) return;
+    const T* r = src + ((m0 + blk) * (int64_t)n + (row - bn)) * n - bn;  // r[c], c in [bn, bn+n)
+    if constexpr (sizeof(T) == 4) {
+        if (n == kTile && (reinterpret_cast<uintptr_t>(r + c0) & 15) == 0) {
+#pragma unroll
+            for (int j = 0; j < 64; j += 4) {
+                const float4 w = *reinterpret_cast<const float4*>(r + c0 + j);
+                v[j] = w.x; v[j + 1] = w.y; v[j + 2] = w.z; v[j + 3] = w.w;
+            }
+            return;
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < 64; ++j)
+        if ((unsigned)(c0 + j - bn) < (unsigned)n) v[j] = Elem<T>::load(r[c0 + j]);
+}
+
+__device__ __forceinline__ float abs_max64(const float (&v)[64]) {
+    float m0 = 0.f, m1 = 0.f;
+#pragma unroll
+    for (int j = 0; j < 64; j += 2) {
+        m0 = fmaxf(m0, fabsf(v[j]));
+        m1 = fmaxf(m1, fabsf(v[j + 1]));
+    }
+    return fmaxf(m0, m1);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kTcThreads, 1)
+ns_tc_bwd_kernel(const T* __restrict__ g, const T* __restrict__ v, T* __restrict__ da, int batch, int n, int nb) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    NsBwdShared& sh = *reinterpret_cast<NsBwdShared*>(base + 4 * kOpBytes);
+    const uint32_t sb = smem_u32(base);  // V hi, V lo, G hi, G lo: 32 KB each
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int quad = warp & 3, half = warp >> 2;
+    const int row = quad * 32 + lane;
+    const int c0 = half * 64;
+    const uint32_t rbase = (uint32_t)(half * 16384 + row * 128);
+    const int rx = row & 7;
+    const int64_t m0 = (int64_t)blockIdx.x * nb;
+    const int nrows = (int)min((int64_t)nb, (int64_t)batch - m0) * n;
+    const bool valid = row < nrows;
+    const int blk = valid ? row / n : -1;
+    const int bn = valid ? blk * n : 0;
+
+    if (tid == 0) {
+        mbar_init(&sh.bar[0], 1);
+        mbar_init(&sh.bar[1], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    for (int e = tid; e < kTile; e += kTcThreads) sh.vmax[e] = sh.gmax[e] = sh.tmax[e] = 0u;
+    if (warp == 0) tmem_alloc(&sh.tmem_base, kTmemCols);
+    uint32_t seg = 0;
+#pragma unroll
+    for (int i = 0; i < 5; ++i) {
+        const int o = __shfl_down_sync(0xffffffffu, blk, 1 << i);
+        if (valid && lane + (1 << i) < 32 && o == blk) seg |= 1u << i;
+    }
+    const int prev = __shfl_up_sync(0xffffffffu, blk, 1);
+    const bool leader = valid && (lane == 0 || prev != blk);
+    const int blk0 = __shfl_sync(0xffffffffu, blk, 0);
+    const bool warp_one = __all_sync(0xffffffffu, valid && blk == blk0);
+
+    // ---- V and G rows, their per-matrix maxima ------------------------------
+    float w[64];
+    load_rows<T>(v, m0, n, valid, blk, bn, row, c0, w);
+    {
+        const float m = seg_max_nn(abs_max64(w), seg, warp_one);
+        if (leader) atomicMax(&sh.vmax[blk], __float_as_uint(m));
+    }
+    __syncthreads();
+    const float sV = valid ? split_scale(__uint_as_float(sh.vmax[blk])) : 1.f;
+    store_v(sb + rbase, rx, w, sV, true);  // V hi at [0,32K), lo at [32K,64K)
+    load_rows<T>(g, m0, n, valid, blk, bn, row, c0, w);
+    {
+        const float m = seg_max_nn(abs_max64(w), seg, warp_one);
+        if (leader) atomicMax(&sh.gmax[blk], __float_as_uint(m));
+    }
+    __syncthreads();
+    const float sG = valid ? split_scale(__uint_as_float(sh.gmax[blk])) : 1.f;
+    store_v(sb + 2 * kOpBytes + rbase, rx, w, sG, true);  // G hi at [64K,96K), lo at [96K,128K)
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    const uint32_t tmem = sh.tmem_base;
+    const uint32_t tl = (uint32_t)(quad * 32) << 16;
+    bool ok = true;
+
+    // ---- T1 = V^T G --------------------------------------------------------
+    if (warp == 0) {
+        tc_fence_after();
+        const uint32_t go = elect_one() ? 1u : 0u;
+        const uint64_t dvh = make_desc(sb, 16384, 1024), dvl = make_desc(sb + kOpBytes, 16384, 1024);
+        const uint64_t dgh = make_desc(sb + 2 * kOpBytes, 16384, 1024), dgl = make_desc(sb + 3 * kOpBytes, 16384, 1024);
+#pragma unroll
+        for (int ks = 0; ks < kTile / 16; ++ks) {
+            const uint64_t o = (uint64_t)(ks * 128);  // K step = 16 rows of both row-major operands
+            mma_f16(tmem, dvh + o, dgh + o, kIdescT1, ks > 0 ? 1u : 0u, go);
+            mma_f16(tmem, dvh + o, dgl + o, kIdescT1, 1u, go);
+            mma_f16(tmem, dvl + o, dgh + o, kIdescT1, 1u, go);
+        }
+        if (go) mma_commit(&sh.bar[0]);
+        __syncwarp();
+    }
+    ok = mbar_wait(&sh.bar[0], 0);
+    ok = !__syncthreads_or(!ok);
+    tc_fence_after();
+    // T1 = acc / (sV sG); its hi/lo parts go to tensor memory as the next A operand
+    float t[64];
+#pragma unroll
+    for (int hc = 0; hc < 4; ++hc) {
+        float av[16];
+        tmem_ld16(tmem + tl + c0 + 16 * hc, av);
+        tmem_wait_ld();
+        reg_fence(av);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) t[16 * hc + j] = av[j];
+    }
+    {
+        const float m = seg_max_nn(abs_max64(t), seg, warp_one);
+        if (leader) atomicMax(&sh.tmax[blk], __float_as_uint(m));
+    }
+    __syncthreads();
+    const float sT = valid ? split_scale(__uint_as_float(sh.tmax[blk])) : 1.f;  // of the accumulator values
+#pragma unroll
+    for (int hc = 0; hc < 4; ++hc) {
+        float p[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) p[j] = t[16 * hc + j];
+        uint32_t pk[8];
+        split_half(p, sT, false, pk);
+        tmem_st8(tmem + tl + kTile + 32 * half + 8 * hc, pk);
+        split_half(p, sT, true, pk);
+        tmem_st8(tmem + tl + kTile + 64 + 32 * half + 8 * hc, pk);
+        tmem_wait_st();
+    }
+    tc_fence_before();
+    __syncthreads();
+    // ---- dA = -T1 V^T ------------------------------------------------------
+    if (warp == 0) {
+        tc_fence_after();
+        const uint32_t el = elect_one() ? 1u : 0u;  // every lane of the warp elects
+        const uint32_t go = ok ? el : 0u;
+        const uint64_t dvh = make_desc(sb, 16, 1024), dvl = make_desc(sb + kOpBytes, 16, 1024);
+#pragma unroll
+        for (int ks = 0; ks < kTile / 16; ++ks) {
+            const uint64_t bo = (uint64_t)((ks >> 2) * 1024 + (ks & 3) * 2);  // K-major: 32 bytes per K step
+            mma_f16_ts(tmem, tmem + kTile + ks * 8, dvh + bo, kIdescDA, ks > 0 ? 1u : 0u, go);
+            mma_f16_ts(tmem, tmem + kTile + ks * 8, dvl + bo, kIdescDA, 1u, go);
+            mma_f16_ts(tmem, tmem + kTile + 64 + ks * 8, dvh + bo, kIdescDA, 1u, go);
+        }
+        if (go) mma_commit(&sh.bar[1]);
+        __syncwarp();
+    }
+    if (ok) ok = mbar_wait(&sh.bar[1], 0);
+    ok = !__syncthreads_or(!ok);
+    tc_fence_after();
+    // acc = T1 V^T * (sV sG) sT sV  ->  dA = -acc / (sV sG sT sV)
+    const float cd = -(1.f / sV) * (1.f / sG) * (1.f / sT) * (1.f / sV);
+#pragma unroll
+    for (int hc = 0; hc < 4; ++hc) {
+        float av[16];
+        tmem_ld16(tmem + tl + c0 + 16 * hc, av);
+        tmem_wait_ld();
+        reg_fence(av);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) t[16 * hc + j] = av[j] * cd;
+    }
+    if (ok && valid) store_rows<T>(da + ((m0 + blk) * (int64_t)n + (row - bn)) * n, c0, bn, n, t);
+    if (!ok && tid == 0) atomicExch(&g_ns_status, (int)LF_ERR_TIMEOUT);
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+size_t tc_bwd_smem_bytes() { return 4 * (size_t)kOpBytes + sizeof(NsBwdShared) + 1024; }
+
+template <typename T>
+int launch_tc_bwd(const void* g, const void* v, void* da, int64_t batch, int64_t n, cudaStream_t st) {
+    const size_t smem = tc_bwd_smem_bytes();
+    if (smem > (size_t)max_optin_smem()) {
+        set_error("NewtonInverse backward tensor-core path needs %zu bytes of shared memory", smem);
+        return LF_ERR_UNSUPPORTED;
+    }
+    const int nb = tc_per_tile(n);
+    const int64_t tiles = (batch + nb - 1) / nb;
+    auto kern = ns_tc_bwd_kernel<T>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    kern<<<(unsigned)tiles, kTcThreads, smem, st>>>(static_cast<const T*>(g), static_cast<const T*>(v),
+                                                   static_cast<T*>(da), (int)batch, (int)n, nb);
+    return check_launch("ns_tc_bwd_kernel");
+}
+
+// ---------------------------------------------------------------------------
+// Matrices with 128 < n <= 256 (fp32) on tcgen05: a cluster of four CTAs per
+// matrix.  The matrix is zero padded to 256 = 2 x 2 blocks of 128; CTA
+// (I, J) (cluster rank 2I + J) owns block (I, J) of H, G, Y and V:
+//   H_IJ = P_I0 V_0J + P_I1 V_1J      A = P rows I (all 256 columns) in tensor memory
+//   G_IJ = delta_IJ - H_IJ
+//   Y_IJ = V_I0 G_0J + V_I1 G_1J      A = V tiles, B = G tiles, shared memory
+//   V_IJ += Y_IJ
+// Each product needs one tile a peer owns: V_(1-I)J for H, V_I(1-J) and
+// G_(1-I)J for Y.  They are pulled over distributed shared memory (mapa +
+// ld.shared::cluster) into local buffers, so no global scratch is needed
+// (the C ABI allocates nothing).  Scales and maxima are per matrix: each CTA
+// reduces its block, the four blocks meet through distributed shared memory
+// after the cluster barriers that already separate the phases.  Every CTA
+// executes every cluster barrier whatever happens to its own waits (a timed
+// out wait only skips MMA work), so no CTA can leave a peer waiting.
+// ---------------------------------------------------------------------------
+constexpr int kC256Threads = 256;
+constexpr int kC256TmemCols = 512;  // accumulator [0,128), P hi [128,256), P lo [256,384)
+// shared memory (from the 1024-aligned base): own V hi/lo [0,64K), peer V
+// hi/lo [64K,128K), own G hi [128K,160K), peer G hi [160K,192K)
+constexpr uint32_t kOwnV = 0, kExtV = 2 * kOpBytes, kOwnG = 4 * kOpBytes, kExtG = 5 * kOpBytes;
+
+struct Ns256Shared {
+    uint64_t bar[2];           // [0]: H complete, [1]: Y complete
+    uint32_t tmem_base;
+    uint32_t gmax[2];          // this CTA's block max|G * sG| (float bits), by iteration parity
+    uint32_t vmax[2];          // this CTA's block max|V| (float bits), by iteration parity
+    uint32_t stat[4];          // set-up, this CTA's rows: max signed row sum (ordered), max |row| sum, max|P|, unused
+    float colpart[2 * kTile];  // set-up: this CTA's |column| sums over its 128 rows, all 256 columns
+};
+
+__device__ __forceinline__ uint32_t cluster_addr(uint32_t local, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ uint32_t ld_cluster_u32(uint32_t addr) {
+    uint32_t v;
+    asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+    return v;
+}
+__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) { return __uint_as_float(ld_cluster_u32(addr)); }
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Copies `bytes` (a multiple of 16 KB) at shared offset `src` of cluster CTA
+// `rank` to local shared offset `dst`; all threads of the CTA take part.
+__device__ __forceinline__ void pull_tile(uint32_t sb, uint32_t dst, uint32_t src, uint32_t rank, int bytes) {
+    const uint32_t rsrc = cluster_addr(sb + src, rank);
+    for (int base = threadIdx.x * 16; base < bytes; base += kC256Threads * 16 * 4) {
+        uint32_t v[4][4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+            asm volatile("ld.shared::cluster.v4.u32 {%0, %1, %2, %3}, [%4];"
+                         : "=r"(v[u][0]), "=r"(v[u][1]), "=r"(v[u][2]), "=r"(v[u][3])
+                         : "r"(rsrc + base + u * kC256Threads * 16)
+                         : "memory");
+#pragma unroll
+        for (int u = 0; u < 4; ++u) sts128(sb + dst + base + u * kC256Threads * 16, v[u][0], v[u][1], v[u][2], v[u][3]);
+    }
+}
+
+// H (+)= sum over the two K blocks of P_I,kb (tensor memory: hi columns
+// a_hi + 64 kb + 8 ks) times V_kb,J (descriptors dvh[kb], dvl[kb]).
+template <bool FULL>
+__device__ __forceinline__ void issue_h256(uint32_t acc, uint32_t a_hi, uint32_t a_lo, const uint64_t (&dvh)[2],
+                                           const uint64_t (&dvl)[2], uint32_t go) {
+#pragma unroll
+    for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+        for (int ks = 0; ks < kTile / 16; ++ks) {
+            const uint32_t ac = 64 * kb + 8 * ks;
+            const uint64_t bo = (uint64_t)(ks * 128);
+            mma_f16_ts(acc, a_hi + ac, dvh[kb] + bo, kIdesc, (kb | ks) ? 1u : 0u, go);
+            if (FULL) {
+                mma_f16_ts(acc, a_hi + ac, dvl[kb] + bo, kIdesc, 1u, go);
+                mma_f16_ts(acc, a_lo + ac, dvh[kb] + bo, kIdesc, 1u, go);
+            }
+        }
+}
+
+// Y (+)= sum over the two K blocks of V_I,kb (K-major, dah[kb] / dal[kb])
+// times G_kb,J (MN-major, dg[kb]).
+template <bool FULL>
+__device__ __forceinline__ void issue_y256(uint32_t acc, const uint64_t (&dah)[2], const uint64_t (&dal)[2],
+                                           const uint64_t (&dg)[2], uint32_t go) {
+#pragma unroll
+    for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+        for (int ks = 0; ks < kTile / 16; ++ks) {
+            const uint64_t ao = (uint64_t)((ks >> 2) * 1024 + (ks & 3) * 2);
+            mma_f16(acc, dah[kb] + ao, dg[kb] + (uint64_t)(ks * 128), kIdesc, (kb | ks) ? 1u : 0u, go);
+            if (FULL) mma_f16(acc, dal[kb] + ao, dg[kb] + (uint64_t)(ks * 128), kIdesc, 1u, go);
+        }
+}
+
+__global__ void __cluster_dims__(4, 1, 1) __launch_bounds__(kC256Threads, 1)
+ns_tc256_fwd_kernel(const float* __restrict__ a, float* __restrict__ x, int n, int iters, int mode, float reg,
+                    int precision) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];  // re-aligned to 1024 below
+    unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    float* stage = reinterpret_cast<float*>(base + kExtV);  // set-up: rows I of P, 128 x 256 fp32 (128 KB)
+    Ns256Shared& sh = *reinterpret_cast<Ns256Shared*>(base + 6 * kOpBytes);
+    const uint32_t sb = smem_u32(base);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int quad = warp & 3, half = warp >> 2;
+    const int row = quad * 32 + lane;  // row of the block (= TMEM lane)
+    const int c0 = half * 64;          // this thread's 64 columns of the block
+    const uint32_t rbase = (uint32_t)(half * 16384 + row * 128);
+    const int rx = row & 7;
+    const uint32_t crank = blockIdx.x & 3u;  // cluster rank = 2 I + J
+    const int I = (int)(crank >> 1), J = (int)(crank & 1);
+    const int64_t mat = blockIdx.x >> 2;
+    const float* A = a + mat * (int64_t)n * n;
+    float* X = x + mat * (int64_t)n * n;
+    const int gi = 128 * I + row;  // matrix row of this thread
+    const bool rvalid = gi < n;
+    const int dchunk = (I == J && (quad >> 1) == half) ? (quad & 1) : -1;  // diagonal chunk (diagonal blocks only)
+    const uint32_t rank_vi = (uint32_t)(2 * (1 - I) + J);  // owner of V_(1-I)J and G_(1-I)J
+    const uint32_t rank_vj = (uint32_t)(2 * I + (1 - J));  // owner of V_I(1-J)
+
+    if (tid == 0) {
+        mbar_init(&sh.bar[0], 1);
+        mbar_init(&sh.bar[1], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        sh.gmax[0] = sh.gmax[1] = sh.vmax[0] = sh.vmax[1] = 0u;
+        sh.stat[0] = sh.stat[1] = sh.stat[2] = sh.stat[3] = 0u;
+    }
+    if (warp == 0) tmem_alloc(&sh.tmem_base, kC256TmemCols);
+
+    // ---- set-up: rows I of P = A + reg I (all 256 columns) into the stage ----
+    // stage row r, column c (0..255) at r*256 + swizzled chunk (16-byte chunks XOR r%32 within each 128-column half)
+    auto st_idx = [](int r, int c) { return r * 256 + (c & 128) + ((((c & 127) >> 2) ^ r) & 31) * 4 + (c & 3); };
+    for (int e = tid; e < kTile * 64; e += kC256Threads) {  // 64 float4 per row
+        const int r = e >> 6, c4 = e & 63, c = 4 * c4;
+        const int i = 128 * I + r;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (i < n) {
+            const float* Ar = A + (int64_t)i * n;
+            float* vp = &v.x;
+            if ((n & 3) == 0 && c + 3 < n) {
+                v = *reinterpret_cast<const float4*>(Ar + c);
+            } else {
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                    if (c + q < n) vp[q] = Ar[c + q];
+            }
+            if (i >= c && i < c + 4) vp[i - c] += reg;
+        }
+        *reinterpret_cast<float4*>(stage + st_idx(r, c)) = v;
+    }
+    __syncthreads();
+    // this CTA's rows: signed row sum, |row| sum, max|P|; |column| partial sums
+    {
+        if (tid < kTile) {
+            float rs = 0.f, ra = 0.f, pm = 0.f;
+            for (int c = 0; c < 2 * kTile; ++c) {
+                const float p = stage[st_idx(tid, c)];
+                rs += p;
+                ra += fabsf(p);
+                pm = fmaxf(pm, fabsf(p));
+            }
+            if (128 * I + tid < n) {
+                atomicMax(&sh.stat[0], ord_bits(rs));
+                atomicMax(&sh.stat[1], __float_as_uint(ra));
+            }
+            atomicMax(&sh.stat[2], __float_as_uint(pm));
+        }
+        for (int c = tid; c < 2 * kTile; c += kC256Threads) {
+            float cs = 0.f;
+            for (int r = 0; r < kTile; ++r) cs += fabsf(stage[st_idx(r, c)]);
+            sh.colpart[c] = cs;
+        }
+    }
+    cluster_sync_all();  // every CTA's statistics are visible to its peers
+    float rsmax = -INFINITY, ramax = 0.f, pmax = 0.f, camax = 0.f;
+    {
+        const uint32_t sst = smem_u32(&sh.stat[0]), scol = smem_u32(&sh.colpart[0]);
+#pragma unroll
+        for (uint32_t rk = 0; rk < 4; ++rk) {
+            rsmax = fmaxf(rsmax, ord_float(ld_cluster_u32(cluster_addr(sst, rk))));
+            ramax = fmaxf(ramax, ld_cluster_f32(cluster_addr(sst + 4, rk)));
+            pmax = fmaxf(pmax, ld_cluster_f32(cluster_addr(sst + 8, rk)));
+        }
+        // full |column| sums = this row half + the other row half (ranks 0/2 hold rows 0..127 / 128..255)
+        for (int c = lane; c < 2 * kTile; c += 32) {
+            const float cs = ld_cluster_f32(cluster_addr(scol + 4 * c, 0)) + ld_cluster_f32(cluster_addr(scol + 4 * c, 2));
+            camax = fmaxf(camax, cs);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) camax = fmaxf(camax, __shfl_xor_sync(0xffffffffu, camax, o));
+    }
+    const float cinit = (mode == LF_NS_INIT_REFERENCE) ? __fdiv_rn(1.8f, rsmax * rsmax) : __fdiv_rn(1.0f, camax * ramax);
+    const float sP = split_scale(pmax);
+    float sV = split_scale(fabsf(cinit) * pmax);
+    const float pinf = ramax;
+    float vmk = fabsf(cinit) * pmax;  // max|V0|
+    const uint32_t tmem = sh.tmem_base;
+    const uint32_t tl = (uint32_t)(quad * 32) << 16;
+    // P rows I as the A operand: K columns kb*128 + c0 + [0,64) of each K block
+#pragma unroll
+    for (int kb = 0; kb < 2; ++kb)
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+            float p[16];
+#pragma unroll
+            for (int q = 0; q < 16; ++q) p[q] = stage[st_idx(row, 128 * kb + c0 + 16 * g + q)];
+            uint32_t pk[8];
+            split_half(p, sP, false, pk);
+            tmem_st8(tmem + tl + kTile + 64 * kb + 32 * half + 8 * g, pk);
+            split_half(p, sP, true, pk);
+            tmem_st8(tmem + tl + 2 * kTile + 64 * kb + 32 * half + 8 * g, pk);
+            tmem_wait_st();
+        }
+    // V0 block (I, J): c P_IJ, or c (P_JI)^T read from the input
+    float V[64];
+#pragma unroll
+    for (int j = 0; j < 64; ++j) {
+        const int gc = 128 * J + c0 + j;
+        float pv;
+        if (mode == LF_NS_INIT_REFERENCE) {
+            pv = stage[st_idx(row, 128 * J + c0 + j)];
+        } else {
+            pv = (rvalid && gc < n) ? A[(int64_t)gc * n + gi] + (gc == gi ? reg : 0.f) : 0.f;
+        }
+        V[j] = cinit * pv;
+    }
+    bool ok = true;
+    if (iters == 0) {
+        if (rvalid)
+            for (int j = 0; j < 64; ++j)
+                if (128 * J + c0 + j < n) X[(int64_t)gi * n + 128 * J + c0 + j] = V[j];
+    } else {
+        tc_fence_before();
+        __syncthreads();  // stage reads done: the stage overlaps the peer buffers
+        store_v(sb + kOwnV + rbase, rx, V, sV, precision == LF_NS_PREC_SPLIT3 || iters <= 2);
+        fence_async_smem();
+        for (int k = 0; k < iters; ++k) {
+            const uint32_t par = (uint32_t)k & 1u;
+            const bool full = precision == LF_NS_PREC_SPLIT3 || k >= iters - 2;
+            const bool last = k == iters - 1;
+            const int vbytes = full ? 2 * kOpBytes : kOpBytes;
+            // ---- pull V_(1-I)J; H = P V -------------------------------------
+            cluster_sync_all();  // X1: every block's V_k (and its max) is complete
+            if (k > 0) {
+                vmk = 0.f;
+#pragma unroll
+                for (uint32_t rk = 0; rk < 4; ++rk)
+                    vmk = fmaxf(vmk, ld_cluster_f32(cluster_addr(smem_u32(&sh.vmax[par]), rk)));
+            }
+            if (tid == 0) sh.gmax[par] = 0u;  // last read by the peers before X1
+            pull_tile(sb, kExtV, kOwnV, rank_vi, vbytes);
+            fence_async_smem();
+            tc_fence_before();
+            __syncthreads();
+            if (warp == 0) {
+                tc_fence_after();
+                const uint32_t el = elect_one() ? 1u : 0u;  // every lane of the warp elects
+                const uint32_t go = ok ? el : 0u;
+                uint64_t dvh[2], dvl[2];
+                dvh[I] = make_desc(sb + kOwnV, 16384, 1024);
+                dvl[I] = make_desc(sb + kOwnV + kOpBytes, 16384, 1024);
+                dvh[1 - I] = make_desc(sb + kExtV, 16384, 1024);
+                dvl[1 - I] = make_desc(sb + kExtV + kOpBytes, 16384, 1024);
+                if (full) issue_h256<true>(tmem, tmem + kTile, tmem + 2 * kTile, dvh, dvl, go);
+                else issue_h256<false>(tmem, tmem + kTile, tmem + 2 * kTile, dvh, dvl, go);
+                if (go) mma_commit(&sh.bar[0]);
+                __syncwarp();
+            }
+            const float sG = split_scale(1.f + pinf * vmk);  // |G_ij| <= 1 + ||P||_inf max|V|
+            const float chs = -sG * (1.f / sP) * (1.f / sV);
+            const uint64_t chs2 = pk2(chs, chs);
+            if (ok) ok = mbar_wait(&sh.bar[0], par);
+            ok = !__syncthreads_or(!ok);
+            tc_fence_after();
+            // ---- G_IJ into the own G buffer --------------------------------
+            __half2 hm = __float2half2_rn(0.f);
+#pragma unroll
+            for (int hc = 0; hc < 4; ++hc) {
+                float av[16];
+                tmem_ld16(tmem + tl + c0 + 16 * hc, av);
+                tmem_wait_ld();
+                reg_fence(av);
+                const uint32_t gh_row = sb + kOwnG + rbase;
+                if ((hc >> 1) == dchunk) g_store<true>(av, chs2, sG, lane, 16 * (hc & 1), hm, gh_row, rx, hc);
+                else g_store<false>(av, chs2, sG, lane, 0, hm, gh_row, rx, hc);
+            }
+            {
+                const float gm = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(fmaxf(__low2float(hm), __high2float(hm)))));
+                if (lane == 0) atomicMax(&sh.gmax[par], __float_as_uint(gm));
+            }
+            tc_fence_before();
+            __syncthreads();  // H consumed; the peer V buffer is free again
+            pull_tile(sb, kExtV, kOwnV, rank_vj, vbytes);  // V_I(1-J)
+            fence_async_smem();
+            // ---- pull G_(1-I)J; Y = V G ----------------------------------------
+            cluster_sync_all();  // X2: every G block and its max are complete; the V pulls are done
+            if (tid == 0) sh.vmax[par ^ 1u] = 0u;  // last read by the peers after the previous X1
+            pull_tile(sb, kExtG, kOwnG, rank_vi, kOpBytes);
+            float gmk = 0.f;
+#pragma unroll
+            for (uint32_t rk = 0; rk < 4; ++rk) gmk = fmaxf(gmk, ld_cluster_f32(cluster_addr(smem_u32(&sh.gmax[par]), rk)));
+            gmk *= 1.f / sG;
+            fence_async_smem();
+            tc_fence_before();
+            __syncthreads();
+            if (warp == 0) {
+                tc_fence_after();
+                const uint32_t el = elect_one() ? 1u : 0u;
+                const uint32_t go = ok ? el : 0u;
+                uint64_t dah[2], dal[2], dg[2];
+                dah[J] = make_desc(sb + kOwnV, 16, 1024);
+                dal[J] = make_desc(sb + kOwnV + kOpBytes, 16, 1024);
+                dah[1 - J] = make_desc(sb + kExtV, 16, 1024);
+                dal[1 - J] = make_desc(sb + kExtV + kOpBytes, 16, 1024);
+                dg[I] = make_desc(sb + kOwnG, 16384, 1024);
+                dg[1 - I] = make_desc(sb + kExtG, 16384, 1024);
+                if (full) issue_y256<true>(tmem, dah, dal, dg, go);
+                else issue_y256<false>(tmem, dah, dal, dg, go);
+                if (go) mma_commit(&sh.bar[1]);
+                __syncwarp();
+            }
+            const float sVn = split_scale(vmk * (1.f + (float)n * gmk));  // max|V + V G| <= max|V| (1 + n max|G|)
+            const uint64_t cy2 = pk2((1.f / sV) * (1.f / sG), (1.f / sV) * (1.f / sG));
+            if (ok) ok = mbar_wait(&sh.bar[1], par);
+            ok = !__syncthreads_or(!ok);
+            tc_fence_after();
+            // ---- V_IJ += Y_IJ ------------------------------------------------
+#pragma unroll
+            for (int hc = 0; hc < 4; ++hc) {
+                float av[16];
+                tmem_ld16(tmem + tl + c0 + 16 * hc, av);
+                tmem_wait_ld();
+                reg_fence(av);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const int j = 16 * hc + 2 * e;
+                    upk2(fma2(pk2(av[2 * e], av[2 * e + 1]), cy2, pk2(V[j], V[j + 1])), V[j], V[j + 1]);
+                }
+            }
+            if (last) {
+                if (ok && rvalid) {
+                    float* xr = X + (int64_t)gi * n;
+                    for (int j = 0; j < 64; ++j)
+                        if (128 * J + c0 + j < n) xr[128 * J + c0 + j] = V[j];
+                }
+            } else {
+                const float vm = store_v(sb + kOwnV + rbase, rx, V, sVn,
+                                         precision == LF_NS_PREC_SPLIT3 || k + 1 >= iters - 2) * (1.f / sVn);
+                const float wm = __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(vm)));
+                if (lane == 0) atomicMax(&sh.vmax[par ^ 1u], __float_as_uint(wm));
+                sV = sVn;
+                fence_async_smem();
+                tc_fence_before();
+            }
+        }
+    }
+    if (!ok && tid == 0) atomicExch(&g_ns_status, (int)LF_ERR_TIMEOUT);
+    tc_fence_before();
+    cluster_sync_all();  // no peer reads this CTA's shared memory any more
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kC256TmemCols);
+    }
+}
+
+size_t tc256_smem_bytes() { return 6 * (size_t)kOpBytes + sizeof(Ns256Shared) + 1024; }
+
+// ---------------------------------------------------------------------------
 // Matrices with 128 < n <= 256 (fp32), CUDA cores.
 // ---------------------------------------------------------------------------
 constexpr int kMaxN = 256;
@@ -1141,6 +1741,19 @@ int launch_big_fwd(const void* a, void* x, int64_t batch, int64_t n, int iters, 
     return check_launch("ns_simt_big_kernel");
 }
 
+int launch_tc256(const float* a, float* x, int64_t batch, int64_t n, int iters, int mode, float reg, int precision,
+                 cudaStream_t st) {
+    const size_t smem = tc256_smem_bytes();
+    if (smem > (size_t)max_optin_smem()) {
+        set_error("NewtonInverse n > 128 tensor-core path needs %zu bytes of shared memory", smem);
+        return LF_ERR_UNSUPPORTED;
+    }
+    if (batch > 0x7fffffffLL / 4) { set_error("batch too large"); return LF_ERR_UNSUPPORTED; }
+    cudaFuncSetAttribute(ns_tc256_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    ns_tc256_fwd_kernel<<<(unsigned)(4 * batch), kC256Threads, smem, st>>>(a, x, (int)n, iters, mode, reg, precision);
+    return check_launch("ns_tc256_fwd_kernel");
+}
+
 template <typename T>
 int launch_bwd_global(const void* g, const void* v, void* da, int64_t batch, int64_t n, cudaStream_t st) {
     using Acc = typename Elem<T>::acc;
@@ -1165,8 +1778,6 @@ __global__ void bounded_wait_probe_kernel(uint64_t limit_ns) {
 
 size_t tc_smem_bytes() { return 3 * (size_t)kOpBytes + sizeof(NsShared) + 1024; }
 
-// Matrices per 128x128 tile: floor(128/n) for n <= 64 (block-diagonal), else 1.
-int tc_per_tile(int64_t n) { return n <= kTile / 2 ? (int)(kTile / n) : 1; }
 
 template <typename T>
 int launch_tc(const T* a, T* x, int64_t batch, int64_t n, int iters, int mode, float reg, int precision,
@@ -1308,7 +1919,9 @@ extern "C" int lf_newton_inverse_fwd_ex(const void* a, void* x, int64_t batch, i
             set_error("NewtonInverse: n=%lld > %d is supported for fp32 only", (long long)n, kTile);
             return LF_ERR_UNSUPPORTED;
         }
-        return launch_big_fwd(a, x, batch, n, iters, init_mode, reg, st);
+        if (precision == LF_NS_PREC_FP32_SIMT) return launch_big_fwd(a, x, batch, n, iters, init_mode, reg, st);
+        return launch_tc256(static_cast<const float*>(a), static_cast<float*>(x), batch, n, iters, init_mode,
+                            (float)reg, precision, st);
     }
     if (dtype == LF_F64) return launch_simt_fwd<double>(a, x, batch, n, iters, init_mode, reg, st);
     if (precision == LF_NS_PREC_FP32_SIMT) {
@@ -1339,6 +1952,12 @@ extern "C" int lf_newton_inverse_bwd(const void* g, const void* v, void* da, int
     if (batch == 0 || n == 0) return LF_OK;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     if (n > kTile) { LF_DISPATCH(dtype, T, return launch_bwd_global<T>(g, v, da, batch, n, st)); }
+    switch (dtype) {  // tensor cores for fp32 / fp16 / bf16; fp64 on CUDA cores
+        case LF_F32: return launch_tc_bwd<float>(g, v, da, batch, n, st);
+        case LF_F16: return launch_tc_bwd<__half>(g, v, da, batch, n, st);
+        case LF_BF16: return launch_tc_bwd<__nv_bfloat16>(g, v, da, batch, n, st);
+        default: break;
+    }
     LF_DISPATCH(dtype, T, return launch_simt_bwd<T>(g, v, da, batch, n, st));
     return LF_OK;
 }

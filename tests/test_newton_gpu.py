@@ -235,3 +235,38 @@ def test_landmark_inverse_fused_rejects_unsupported(cuda):
     L = torch.randn(1, 16, 8, device=cuda)
     with pytest.raises(RuntimeError, match="precision"):
         capi.laplace_newton_inverse_fwd(L, -0.1, 5, precision=capi.PREC_FP32_SIMT)
+
+
+@pytest.mark.parametrize("n", [5, 49, 64, 100])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16], ids=str)
+def test_backward_tensor_core_packed_tiles(cuda, n, dtype):
+    # n <= 64 packs floor(128/n) matrices per tile (per-matrix scales); a
+    # ragged last tile (batch not a multiple of the packing) is included.
+    g0 = torch.Generator().manual_seed(200 + n)
+    batch = 7
+    V = (torch.randn(1, batch, n, n, generator=g0, dtype=torch.float64) * torch.logspace(-3, 3, batch, dtype=torch.float64).view(1, batch, 1, 1)).to(dtype)
+    G = torch.randn(1, batch, n, n, generator=g0, dtype=torch.float64).to(dtype)
+    dA = capi.newton_inverse_bwd(G.to(cuda), V.to(cuda))
+    torch.cuda.synchronize()
+    ref = O.newton_bwd(G.float().numpy(), V.float().numpy())
+    tol = 1e-5 if dtype == torch.float32 else 1e-2
+    for b in range(batch):  # per matrix: magnitudes differ by 10^6 across the batch
+        r = ref[0, b]
+        np.testing.assert_allclose(dA[0, b].float().cpu().numpy(), r, rtol=0, atol=tol * 4 * np.abs(r).max())
+
+
+@pytest.mark.parametrize("n", [129, 256])
+def test_forward_large_n_mixed_zero_iters_and_simt(cuda, n):
+    A = spd(3, n, seed=300 + n)
+    Ad = A.to(cuda)
+    X0 = capi.newton_inverse_fwd(Ad, 0)
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(X0.cpu().numpy(), O.newton_fwd(A.numpy(), 0, order=1), rtol=1e-6, atol=1e-9)
+    Xr = O.newton_fwd(A.numpy(), 10, order=1)
+    r_ref = _res(A.numpy(), Xr, 0.01)
+    for prec in (capi.PREC_MIXED, capi.PREC_FP32_SIMT):
+        X = capi.newton_inverse_fwd(Ad, 10, precision=prec)
+        torch.cuda.synchronize()
+        assert capi.device_status() == 0
+        r_gpu = _res(A.numpy(), X.cpu().numpy(), 0.01)
+        assert np.all(np.abs(r_gpu - r_ref) <= 1e-4), (prec, r_gpu, r_ref)
