@@ -49,23 +49,23 @@ inline double wave_efficiency(int64_t total, int64_t slots) {
 }
 
 template <typename K>
-int64_t cta_slots(K kern, size_t smem) {
+int64_t cta_slots(K kern, size_t smem, int threads = kThreads) {
     // The occupancy query costs microseconds of host time per launch, so the
     // answer is cached per (kernel, device, shared-memory size).  Launchers
     // that compare two kernels query both on every call, so the cache keeps
     // every key rather than only the last one.
     static std::mutex mu;
-    static std::map<std::tuple<const void*, int, size_t>, int> cache;
+    static std::map<std::tuple<const void*, int, size_t, int>, int> cache;
     int dev = 0;
     cudaGetDevice(&dev);
-    const auto key = std::make_tuple(reinterpret_cast<const void*>(kern), dev, smem);
+    const auto key = std::make_tuple(reinterpret_cast<const void*>(kern), dev, smem, threads);
     {
         std::lock_guard<std::mutex> lock(mu);
         auto it = cache.find(key);
         if (it != cache.end()) return (int64_t)it->second * num_sms();
     }
     int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem) != cudaSuccess || per_sm < 1)
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem) != cudaSuccess || per_sm < 1)
         per_sm = 1;
     std::lock_guard<std::mutex> lock(mu);
     cache[key] = per_sm;
@@ -355,6 +355,18 @@ int launch_fwd_mc(const T* q, const T* kT, T* s, int64_t bh, int64_t n, int64_t 
                   cudaStream_t st, double escale, bool do_exp) {
     size_t smem = fwd_smem_total<T, TM, MC, DR>(m, d);
     int gw = fwd_stage_width<T, TM, MC>(m);
+    {
+        // Narrower landmark groups when that lets two CTAs share an SM (the
+        // staged K^T and the output tile of one CTA otherwise fill more than
+        // half of its shared memory, leaving 8 warps per SM).
+        const size_t half_sm = (size_t)max_optin_smem() / 2 - 1024;
+        const size_t ksb = (fwd_smem<T, TM, MC, DR>(m, d) + 15) & ~(size_t)15;
+        const size_t row_bytes = (size_t)kThreads * TM * sizeof(T);
+        if (gw > 0 && smem > half_sm && ksb + 2 * MC * row_bytes <= half_sm) {
+            gw = (int)(((half_sm - ksb) / row_bytes) / MC * MC);
+            smem = ksb + (size_t)gw * row_bytes;
+        }
+    }
     if (gw == 0 || smem > (size_t)max_optin_smem()) {
         gw = 0;
         smem = fwd_smem<T, TM, MC, DR>(m, d);
@@ -1114,28 +1126,27 @@ int launch_bwd_flat_t(const void* g, const void* q, const void* kT, void* dq, vo
 // landmark chunks and dK partials of the row groups are combined in a fixed
 // order (bitwise reproducible); the row-split CTAs of one (b,h) form a
 // cluster and add their dK through distributed shared memory.
-template <typename T, int DBT, int MCNT>
-__global__ void __launch_bounds__(kThreads, 1)
+template <typename T, int DBT, int MCNT, int MB, int NT>
+__global__ void __launch_bounds__(NT, 1)
 lsub_bwd_wide_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* __restrict__ kT,
                      T* __restrict__ dq, T* __restrict__ dk, BwdGeom geo) {
     using A = typename Elem<T>::acc;
-    constexpr int MB = 64;
     constexpr int MPT = MB * MCNT;             // padded landmarks
     constexpr int CW = 32 * DBT;               // channels per CTA
-    constexpr int RG = (kThreads / 32) / (DBT * MCNT);
+    constexpr int RG = (NT / 32) / (DBT * MCNT);
     constexpr int RC = 4096 / MPT;             // staged rows per chunk (16 values per thread)
-    constexpr int GPT = RC * MPT / kThreads;   // dS values staged per thread (= 16)
-    constexpr int QPT = RC * CW / kThreads;    // Q values staged per thread
+    constexpr int GPT = RC * MPT / NT;   // dS values staged per thread
+    constexpr int QPT = RC * CW / NT;    // Q values staged per thread
     constexpr int WPR = MPT / 32;              // warps spanning one staged row
-    static_assert(RG >= 1 && GPT == 16 && QPT >= 1, "bad wide backward shape");
+    static_assert(RG >= 1 && GPT >= 1 && QPT >= 1 && NT % MPT == 0, "bad wide backward shape");
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const int n = geo.n, m = geo.m, d = geo.d, KSTR = geo.KSTR;
     A* gs = reinterpret_cast<A*>(smem_raw);        // [RC][MPT]
     A* qs = gs + RC * MPT;                          // [RC][CW]
     A* rpart = qs + RC * CW;                        // [RC][WPR]
     A* csum = rpart + RC * WPR;                     // [MPT]
-    A* cpart = csum + MPT;                          // [kThreads / MPT][MPT]
-    A* dqp = cpart + (kThreads / MPT) * MPT;        // [MCNT][RC][CW]
+    A* cpart = csum + MPT;                          // [NT / MPT][MPT]
+    A* dqp = cpart + (NT / MPT) * MPT;        // [MCNT][RC][CW]
     A* dkb = dqp + MCNT * RC * CW;                  // [CW][KSTR]
     A* dpart = dkb + CW * KSTR;                     // [RG][CW][KSTR] (RG > 1)
 
@@ -1148,7 +1159,7 @@ lsub_bwd_wide_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* 
     const bool lane_active = c < d;
     const int j0 = mcb * MB;
     const int sj = tid % MPT, srow0 = tid / MPT;    // staging column / first row
-    constexpr int SRS = kThreads / MPT;             // staging row stride
+    constexpr int SRS = NT / MPT;             // staging row stride
 
     const T* Gb = g + (int64_t)bh * n * m;
     const T* Qb = q + (int64_t)bh * n * d;
@@ -1175,7 +1186,7 @@ lsub_bwd_wide_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* 
         }
 #pragma unroll
         for (int k = 0; k < QPT; ++k) {
-            const int e = tid + kThreads * k;
+            const int e = tid + NT * k;
             const int i = e / CW, x = e % CW;
             const int64_t row = rc + i;
             pq[k] = (row < r_end && x < d) ? Elem<T>::load(Qb[row * d + x]) : A(0);
@@ -1197,7 +1208,7 @@ lsub_bwd_wide_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* 
             if (lane == 0) rpart[i * WPR + (sj >> 5)] = rs;
         }
 #pragma unroll
-        for (int k = 0; k < QPT; ++k) qs[tid + kThreads * k] = pq[k];
+        for (int k = 0; k < QPT; ++k) qs[tid + NT * k] = pq[k];
         __syncthreads();
         if (rc + RC < r_end) load_chunk(rc + RC);
 
@@ -1234,7 +1245,7 @@ lsub_bwd_wide_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* 
         }
         __syncthreads();
         // dQ = 2 * sum over landmark chunks (fixed order) - row sum of dS
-        for (int e = tid; e < rows * CW; e += kThreads) {
+        for (int e = tid; e < rows * CW; e += NT) {
             const int i = e / CW, x = e % CW;
             if (x >= d) continue;
             A acc = A(0);
@@ -1260,13 +1271,13 @@ lsub_bwd_wide_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* 
         }
     }
     __syncthreads();
-    for (int j = tid; j < m; j += kThreads) {
+    for (int j = tid; j < m; j += NT) {
         A s = A(0);
         for (int r = 0; r < SRS; ++r) s += cpart[r * MPT + j];
         csum[j] = s;
     }
     __syncthreads();
-    for (int e = tid; e < CW * m; e += kThreads) {
+    for (int e = tid; e < CW * m; e += NT) {
         const int cc = e / m, j = e % m;
         if (cc >= d) continue;
         A s = csum[j];
@@ -1284,7 +1295,7 @@ lsub_bwd_wide_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* 
     const int per = (total + cs - 1) / cs;
     const int e0 = rank * per, e1 = min(total, e0 + per);
     T* dkout = dk + (int64_t)bh * d * m;
-    for (int e = e0 + tid; e < e1; e += kThreads) {
+    for (int e = e0 + tid; e < e1; e += NT) {
         const int cc = e / m, j = e - cc * m;
         A s = A(0);
         for (int r = 0; r < cs; ++r) {
@@ -1296,25 +1307,25 @@ lsub_bwd_wide_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* 
     cluster.sync();
 }
 
-template <typename T, int DBT, int MCNT>
+template <typename T, int DBT, int MCNT, int MB = 64, int NT = kThreads>
 int launch_bwd_wide(const T* g, const T* q, const T* kT, T* dq, T* dk, int64_t bh, int64_t n, int64_t m,
                     int64_t d, cudaStream_t st) {
     using A = typename Elem<T>::acc;
-    constexpr int MPT = 64 * MCNT, CW = 32 * DBT, RG = 8 / (DBT * MCNT), RC = 4096 / MPT;
+    constexpr int MPT = MB * MCNT, CW = 32 * DBT, RG = (NT / 32) / (DBT * MCNT), RC = 4096 / MPT;
     BwdGeom geo;
     geo.n = (int)n; geo.m = (int)m; geo.d = (int)d;
     geo.DBC = DBT; geo.MCN = MCNT; geo.RG = RG; geo.MP = MPT; geo.RC = RC;
     geo.KSTR = (int)(m | 1);
     size_t smem = sizeof(A) * ((size_t)RC * MPT + (size_t)RC * CW + (size_t)RC * (MPT / 32) + MPT +
-                               (size_t)(kThreads / MPT) * MPT + (size_t)MCNT * RC * CW + (size_t)CW * geo.KSTR +
+                               (size_t)(NT / MPT) * MPT + (size_t)MCNT * RC * CW + (size_t)CW * geo.KSTR +
                                (RG > 1 ? (size_t)RG * CW * geo.KSTR : 0));
     if (smem > (size_t)max_optin_smem()) {
         set_error("LaplaceSubtraction backward: needs %zu bytes of shared memory", smem);
         return LF_ERR_UNSUPPORTED;
     }
-    auto kern = lsub_bwd_wide_kernel<T, DBT, MCNT>;
+    auto kern = lsub_bwd_wide_kernel<T, DBT, MCNT, MB, NT>;
     if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    const int64_t slots = cta_slots(kern, smem);
+    const int64_t slots = cta_slots(kern, smem, NT);
     const int64_t max_by_rows = (n + RC - 1) / RC;
     int64_t cs = 1;
     double best = -1.0;
@@ -1328,7 +1339,7 @@ int launch_bwd_wide(const T* g, const T* q, const T* kT, T* dq, T* dk, int64_t b
     if (bh > 65535) { set_error("b*h = %lld exceeds 65535", (long long)bh); return LF_ERR_UNSUPPORTED; }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)cs, (unsigned)bh, 1);
-    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.blockDim = dim3(NT, 1, 1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -1468,7 +1479,9 @@ int launch_bwd_t(const void* g, const void* q, const void* kT, void* dq, void* d
             }
             if (mc == 1) return launch_bwd_wide<T, 2, 1>(G, Q, K, DQp, DKp, bh, n, m, d, st);
             if (mc == 2) return launch_bwd_wide<T, 2, 2>(G, Q, K, DQp, DKp, bh, n, m, d, st);
-            return launch_bwd_wide<T, 2, 4>(G, Q, K, DQp, DKp, bh, n, m, d, st);
+            // 128 < m <= 256: 32 landmarks per warp, 16 warps (half the
+            // registers per thread of 64-landmark warps, twice the warps per SM)
+            return launch_bwd_wide<T, 2, 8, 32, 2 * kThreads>(G, Q, K, DQp, DKp, bh, n, m, d, st);
         }
     }
     int mcn = 1;

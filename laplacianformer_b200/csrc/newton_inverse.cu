@@ -188,6 +188,13 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
           "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
         : "r"(taddr));
 }
+// 32 lanes x 8 consecutive 32-bit columns.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
+    uint32_t* r = reinterpret_cast<uint32_t*>(v);
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
+}
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 // Ties registers written by tcgen05.ld to a point after tcgen05.wait::ld so
 // that the compiler cannot hoist their uses above the wait.
@@ -704,14 +711,14 @@ ns_tc_fwd_kernel(const T* __restrict__ a, T* __restrict__ x, int batch, int n, i
             tc_fence_after();
             // ---- V <- V + Y ------------------------------------------------------
 #pragma unroll
-            for (int hc = 0; hc < 4; ++hc) {
-                float av[16];
-                tmem_ld16(tmem + tl + c0 + 16 * hc, av);
+            for (int hc = 0; hc < 8; ++hc) {
+                float av[8];
+                tmem_ld8(tmem + tl + c0 + 8 * hc, av);
                 tmem_wait_ld();
                 reg_fence(av);
 #pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    const int j = 16 * hc + 2 * e;
+                for (int e = 0; e < 4; ++e) {
+                    const int j = 8 * hc + 2 * e;
                     upk2(fma2(pk2(av[2 * e], av[2 * e + 1]), cy2, pk2(V[j], V[j + 1])), V[j], V[j + 1]);
                 }
             }

@@ -19,6 +19,8 @@ SHAPES = [
     (1, 1, 37, 48, 9),       # non power-of-two channels
     (3, 1, 9, 100, 256),     # many landmarks, d > 64
     (1, 1, 1500, 8, 196),    # m = 196 (landmark-vs-key shape)
+    (1, 2, 300, 64, 256),    # configuration-5 channels / landmarks (16-warp wide backward)
+    (2, 1, 77, 40, 131),     # ragged channels and landmarks on the same path
 ]
 
 
