@@ -32,6 +32,22 @@ inline void LaplaceKernel_forward(const at::Tensor query, const at::Tensor key, 
     AT_ERROR("Not implemented on the CPU");
 }
 
+// Gradients of output = exp(scale * LaplaceSub(query, key)) from gradOutput:
+// dS = scale * output * gradOutput is formed inside the backward kernel
+// (never stored).  Either gradient may be undefined.  No counterpart in the
+// reference.
+void LaplaceKernel_backward_cuda(const at::Tensor gradOutput, const at::Tensor output, double scale,
+                                 const at::Tensor query, const at::Tensor key, at::Tensor gradQuery,
+                                 at::Tensor gradKey);
+
+inline void LaplaceKernel_backward(const at::Tensor gradOutput, const at::Tensor output, double scale,
+                                   const at::Tensor query, const at::Tensor key, at::Tensor gradQuery,
+                                   at::Tensor gradKey) {
+    if (query.is_cuda() && key.is_cuda())
+        return LaplaceKernel_backward_cuda(gradOutput, output, scale, query, key, gradQuery, gradKey);
+    AT_ERROR("Not implemented on the CPU");
+}
+
 inline void LaplaceSubtraction_forward(const at::Tensor query, const at::Tensor key, at::Tensor output) {
     if (query.is_cuda() && key.is_cuda()) return LaplaceSubtraction_forward_cuda(query, key, output);
     AT_ERROR("Not implemented on the CPU");

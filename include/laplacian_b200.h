@@ -109,6 +109,22 @@ LF_API int lf_laplace_kernel_fwd(const void* q, const void* kT, void* kmat,
                           int64_t bh, int64_t n, int64_t m, int64_t d,
                           int dtype, double scale, lf_stream_t stream);
 
+/* Gradients of Kmat = exp(scale * S) (lf_laplace_kernel_fwd) from the
+   upstream gradient GK = dKmat: dS = scale * Kmat * GK is formed inside the
+   backward kernels while they stage their gradient tile (in the accumulation
+   type), then dQ and dKT follow as in lf_laplace_sub_bwd; dS is never
+   written to or read from memory.  kmat is the forward's output.  Either of
+   dq, dkT may be NULL.  `workspace` (NULL, or at least
+   lf_laplace_sub_bwd_workspace_size bytes, 16-byte aligned) selects the
+   balanced launch of lf_laplace_sub_bwd_ws when both gradients are asked
+   for.  No counterpart in the reference (its attention forms dS with
+   separate PyTorch ops before LaplaceSubtraction_backward_query/_key). */
+LF_API int lf_laplace_kernel_bwd(const void* gk, const void* kmat, const void* q, const void* kT,
+                          void* dq, void* dkT,
+                          int64_t bh, int64_t n, int64_t m, int64_t d,
+                          int dtype, double scale, void* workspace, size_t workspace_bytes,
+                          lf_stream_t stream);
+
 /* dQ[b,i,c] = sum_j G[b,i,j] * sign(Q[b,i,c] - KT[b,c,j]), sign(0) = 0.
    Replaces laplace::LaplaceSubtraction_backward_query_cuda
    (src/LaplaceSubtraction_cuda.cu:69-84 -> src/LaplaceSubtraction_cuda_kernel.cu:487-547). */

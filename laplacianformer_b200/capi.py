@@ -34,6 +34,7 @@ SIGNATURES = {
     "lf_version": (_I, []),
     "lf_laplace_sub_fwd": (_I, [_P, _P, _P, _I64, _I64, _I64, _I64, _I, _P]),
     "lf_laplace_kernel_fwd": (_I, [_P, _P, _P, _I64, _I64, _I64, _I64, _I, _D, _P]),
+    "lf_laplace_kernel_bwd": (_I, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I, _D, _P, ctypes.c_size_t, _P]),
     "lf_laplace_sub_bwd_query": (_I, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I, _P]),
     "lf_laplace_sub_bwd_key": (_I, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I, _P]),
     "lf_laplace_sub_bwd": (_I, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I, _P]),
@@ -133,6 +134,20 @@ def laplace_kernel_fwd(q, kT, scale, out=None):
     _check(lib().lf_laplace_kernel_fwd(_ptr(q), _ptr(kT), _ptr(out), bh, n, m, d, dtype_code(q), float(scale),
                                        _stream(q)), "lf_laplace_kernel_fwd")
     return out
+
+
+def laplace_kernel_bwd(gk, kmat, q, kT, scale, dq=None, dk=None, workspace=None):
+    """Gradients of Kmat = exp(scale * LaplaceSub(q, kT)) from dKmat = gk, with
+    dS = scale * Kmat * gk formed inside the backward kernel."""
+    _need_cuda(gk, kmat, q, kT, dq, dk, workspace)
+    bh, n, m, d = _dims(q, kT)
+    dq = torch.empty_like(q) if dq is None else dq
+    dk = torch.empty_like(kT) if dk is None else dk
+    ws_ptr, ws_bytes = (None, 0) if workspace is None else (_ptr(workspace), workspace.numel() * workspace.element_size())
+    _check(lib().lf_laplace_kernel_bwd(_ptr(gk), _ptr(kmat), _ptr(q), _ptr(kT), _ptr(dq), _ptr(dk), bh, n, m, d,
+                                       dtype_code(q), float(scale), ws_ptr, ws_bytes, _stream(q)),
+           "lf_laplace_kernel_bwd")
+    return dq, dk
 
 
 def laplace_sub_bwd_workspace_size(q, kT):

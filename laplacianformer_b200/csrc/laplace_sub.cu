@@ -553,7 +553,28 @@ struct BwdGeom {
     // kRowChunk rows (U = chunks per (b,h)) are dealt out as contiguous runs
     // of P chunks per CTA.
     int64_t U, P, total;
+    // Laplacian-kernel backward: when km is set, the upstream gradient is
+    // dKmat and the kernels stage dS = kscale * km * dKmat (km = exp(kscale *
+    // S), same layout as dS) as they load it.
+    const void* km = nullptr;
+    float kscale = 0.f;
 };
+
+// The optional dS factor of the Laplacian-kernel backward (see BwdGeom::km).
+struct GFuse {
+    const void* km = nullptr;
+    float kscale = 0.f;
+};
+
+// dS value at index e of the (b,h) slice: g[e], or kscale * km[e] * g[e].
+template <typename T>
+__device__ __forceinline__ typename Elem<T>::acc grad_at(const T* __restrict__ gb, const T* __restrict__ kmb,
+                                                         float kscale, int64_t e) {
+    using A = typename Elem<T>::acc;
+    A v = Elem<T>::load(gb[e]);
+    if (kmb) v = (v * Elem<T>::load(kmb[e])) * (A)kscale;
+    return v;
+}
 
 // grid = (cs, bh, channel groups), cluster = (cs, 1, 1).  CTA x of (b,h)
 // handles query rows [x*rows_per_cta, (x+1)*rows_per_cta) for channels
@@ -636,12 +657,13 @@ lsub_bwd_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* __res
         for (int i = warp; i < RC; i += kThreads / 32) {
             const bool row_ok = i < rows;
             const T* grow = Gb + (rc + i) * m;
+            const T* kmrow = geo.km ? static_cast<const T*>(geo.km) + (grow - g) : nullptr;
             A rs = A(0);
 #pragma unroll
             for (int u = 0; u < kMaxColChunks; ++u) {
                 const int j = lane + 32 * u;
                 if (j < MP) {
-                    A v = (row_ok && j < m) ? Elem<T>::load(grow[j]) : A(0);
+                    A v = (row_ok && j < m) ? grad_at<T>(grow, kmrow, geo.kscale, j) : A(0);
                     gs[i * MP + j] = v + v;
                     rs += v;
                     if (DK) cpart[warp * MP + j] += v;
@@ -825,8 +847,9 @@ lsub_bwd_fast_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* 
         const int64_t row = rc + sr;
         const bool ok = row < r_end;
         const T* grow = Gb + row * m + sq * CPT;
+        const T* kmrow = geo.km ? static_cast<const T*>(geo.km) + (grow - g) : nullptr;
 #pragma unroll
-        for (int k = 0; k < CPT; ++k) pg[k] = (ok && sq * CPT + k < m) ? Elem<T>::load(grow[k]) : A(0);
+        for (int k = 0; k < CPT; ++k) pg[k] = (ok && sq * CPT + k < m) ? grad_at<T>(grow, kmrow, geo.kscale, k) : A(0);
         const T* qrow = Qb + row * d + sq * 8;
         if (qvec && ok) {  // d == 32, 16-byte aligned rows: the eight values in one or two 16-byte loads
             if constexpr (sizeof(T) == 4) {
@@ -1008,10 +1031,11 @@ lsub_bwd_dk_finalize(const float* __restrict__ ws, T* __restrict__ dk, int d, in
 
 template <typename T, int MB, bool DQ, bool DK>
 int launch_bwd_fast(const T* g, const T* q, const T* kT, T* dq, T* dk, int64_t bh, int64_t n, int64_t m,
-                    int64_t d, cudaStream_t st) {
+                    int64_t d, cudaStream_t st, GFuse fz = {}) {
     using A = typename Elem<T>::acc;
     BwdGeom geo;
     geo.n = (int)n; geo.m = (int)m; geo.d = (int)d;
+    geo.km = fz.km; geo.kscale = fz.kscale;
     geo.DBC = 1; geo.MCN = 1; geo.RG = kThreads / 32; geo.MP = MB; geo.RC = kRowChunk;
     geo.KSTR = (int)(m | 1);
     size_t smem = sizeof(A) * ((size_t)kRowChunk * MB + (size_t)kRowChunk * 32 + kRowChunk + MB +
@@ -1057,10 +1081,11 @@ int launch_bwd_fast(const T* g, const T* q, const T* kT, T* dq, T* dk, int64_t b
 // than needed.
 template <typename T, int MB>
 int launch_bwd_flat(const T* g, const T* q, const T* kT, T* dq, T* dk, int64_t bh, int64_t n, int64_t m,
-                    int64_t d, float* ws, size_t ws_bytes, size_t* need, cudaStream_t st) {
+                    int64_t d, float* ws, size_t ws_bytes, size_t* need, cudaStream_t st, GFuse fz = {}) {
     using A = typename Elem<T>::acc;
     BwdGeom geo;
     geo.n = (int)n; geo.m = (int)m; geo.d = (int)d;
+    geo.km = fz.km; geo.kscale = fz.kscale;
     geo.DBC = 1; geo.MCN = 1; geo.RG = kThreads / 32; geo.MP = MB; geo.RC = kRowChunk;
     geo.KSTR = (int)(m | 1);
     geo.rows_per_cta = 0;
@@ -1092,7 +1117,8 @@ int launch_bwd_flat(const T* g, const T* q, const T* kT, T* dq, T* dk, int64_t b
 
 template <typename T>
 int launch_bwd_flat_t(const void* g, const void* q, const void* kT, void* dq, void* dk, int64_t bh, int64_t n,
-                      int64_t m, int64_t d, void* ws, size_t ws_bytes, size_t* need, cudaStream_t st) {
+                      int64_t m, int64_t d, void* ws, size_t ws_bytes, size_t* need, cudaStream_t st,
+                      GFuse fz = {}) {
     if (need) *need = 0;
     if constexpr (sizeof(T) == 8) {
         return LF_OK;
@@ -1106,12 +1132,12 @@ int launch_bwd_flat_t(const void* g, const void* q, const void* kT, void* dq, vo
         float* W = static_cast<float*>(ws);
         const int64_t m4 = (m + 3) & ~3;
         switch (m4 <= 16 ? 16 : (m4 <= 32 ? 32 : (m4 <= 48 ? 48 : (m4 <= 52 ? 52 : (m4 <= 56 ? 56 : 64))))) {
-            case 16: return launch_bwd_flat<T, 16>(G, Q, K, DQp, DKp, bh, n, m, d, W, ws_bytes, need, st);
-            case 32: return launch_bwd_flat<T, 32>(G, Q, K, DQp, DKp, bh, n, m, d, W, ws_bytes, need, st);
-            case 48: return launch_bwd_flat<T, 48>(G, Q, K, DQp, DKp, bh, n, m, d, W, ws_bytes, need, st);
-            case 52: return launch_bwd_flat<T, 52>(G, Q, K, DQp, DKp, bh, n, m, d, W, ws_bytes, need, st);
-            case 56: return launch_bwd_flat<T, 56>(G, Q, K, DQp, DKp, bh, n, m, d, W, ws_bytes, need, st);
-            default: return launch_bwd_flat<T, 64>(G, Q, K, DQp, DKp, bh, n, m, d, W, ws_bytes, need, st);
+            case 16: return launch_bwd_flat<T, 16>(G, Q, K, DQp, DKp, bh, n, m, d, W, ws_bytes, need, st, fz);
+            case 32: return launch_bwd_flat<T, 32>(G, Q, K, DQp, DKp, bh, n, m, d, W, ws_bytes, need, st, fz);
+            case 48: return launch_bwd_flat<T, 48>(G, Q, K, DQp, DKp, bh, n, m, d, W, ws_bytes, need, st, fz);
+            case 52: return launch_bwd_flat<T, 52>(G, Q, K, DQp, DKp, bh, n, m, d, W, ws_bytes, need, st, fz);
+            case 56: return launch_bwd_flat<T, 56>(G, Q, K, DQp, DKp, bh, n, m, d, W, ws_bytes, need, st, fz);
+            default: return launch_bwd_flat<T, 64>(G, Q, K, DQp, DKp, bh, n, m, d, W, ws_bytes, need, st, fz);
         }
     }
 }
@@ -1182,7 +1208,9 @@ lsub_bwd_wide_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* 
 #pragma unroll
         for (int k = 0; k < GPT; ++k) {
             const int64_t row = rc + srow0 + SRS * k;
-            pg[k] = (row < r_end && sj < m) ? Elem<T>::load(Gb[row * m + sj]) : A(0);
+            pg[k] = (row < r_end && sj < m)
+                        ? grad_at<T>(Gb, geo.km ? static_cast<const T*>(geo.km) + (Gb - g) : nullptr, geo.kscale, row * m + sj)
+                        : A(0);
         }
 #pragma unroll
         for (int k = 0; k < QPT; ++k) {
@@ -1309,11 +1337,12 @@ lsub_bwd_wide_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* 
 
 template <typename T, int DBT, int MCNT, int MB = 64, int NT = kThreads>
 int launch_bwd_wide(const T* g, const T* q, const T* kT, T* dq, T* dk, int64_t bh, int64_t n, int64_t m,
-                    int64_t d, cudaStream_t st) {
+                    int64_t d, cudaStream_t st, GFuse fz = {}) {
     using A = typename Elem<T>::acc;
     constexpr int MPT = MB * MCNT, CW = 32 * DBT, RG = (NT / 32) / (DBT * MCNT), RC = 4096 / MPT;
     BwdGeom geo;
     geo.n = (int)n; geo.m = (int)m; geo.d = (int)d;
+    geo.km = fz.km; geo.kscale = fz.kscale;
     geo.DBC = DBT; geo.MCN = MCNT; geo.RG = RG; geo.MP = MPT; geo.RC = RC;
     geo.KSTR = (int)(m | 1);
     size_t smem = sizeof(A) * ((size_t)RC * MPT + (size_t)RC * CW + (size_t)RC * (MPT / 32) + MPT +
@@ -1381,10 +1410,11 @@ int pick_mb(int64_t m, int& mcn) {
 
 template <typename T, int MB, bool DQ, bool DK, int MINB>
 int launch_bwd_mb(const T* g, const T* q, const T* kT, T* dq, T* dk, int64_t bh, int64_t n,
-                  int64_t m, int64_t d, int mcn, cudaStream_t st) {
+                  int64_t m, int64_t d, int mcn, cudaStream_t st, GFuse fz = {}) {
     using A = typename Elem<T>::acc;
     BwdGeom geo;
     geo.n = (int)n; geo.m = (int)m; geo.d = (int)d;
+    geo.km = fz.km; geo.kscale = fz.kscale;
     const int DB = (int)((d + 31) / 32);
     geo.MCN = mcn;
     geo.DBC = (kThreads / 32) / mcn;
@@ -1449,7 +1479,7 @@ int launch_bwd_mb(const T* g, const T* q, const T* kT, T* dq, T* dk, int64_t bh,
 
 template <typename T, bool DQ, bool DK>
 int launch_bwd_t(const void* g, const void* q, const void* kT, void* dq, void* dk, int64_t bh,
-                 int64_t n, int64_t m, int64_t d, cudaStream_t st) {
+                 int64_t n, int64_t m, int64_t d, cudaStream_t st, GFuse fz = {}) {
     const T* G = static_cast<const T*>(g);
     const T* Q = static_cast<const T*>(q);
     const T* K = static_cast<const T*>(kT);
@@ -1460,12 +1490,12 @@ int launch_bwd_t(const void* g, const void* q, const void* kT, void* dq, void* d
         if (d <= 32 && m <= 64) {
             const int64_t m4 = (m + 3) & ~3;
             switch (m4 <= 16 ? 16 : (m4 <= 32 ? 32 : (m4 <= 48 ? 48 : (m4 <= 52 ? 52 : (m4 <= 56 ? 56 : 64))))) {
-                case 16: return launch_bwd_fast<T, 16, DQ, DK>(G, Q, K, DQp, DKp, bh, n, m, d, st);
-                case 32: return launch_bwd_fast<T, 32, DQ, DK>(G, Q, K, DQp, DKp, bh, n, m, d, st);
-                case 48: return launch_bwd_fast<T, 48, DQ, DK>(G, Q, K, DQp, DKp, bh, n, m, d, st);
-                case 52: return launch_bwd_fast<T, 52, DQ, DK>(G, Q, K, DQp, DKp, bh, n, m, d, st);
-                case 56: return launch_bwd_fast<T, 56, DQ, DK>(G, Q, K, DQp, DKp, bh, n, m, d, st);
-                default: return launch_bwd_fast<T, 64, DQ, DK>(G, Q, K, DQp, DKp, bh, n, m, d, st);
+                case 16: return launch_bwd_fast<T, 16, DQ, DK>(G, Q, K, DQp, DKp, bh, n, m, d, st, fz);
+                case 32: return launch_bwd_fast<T, 32, DQ, DK>(G, Q, K, DQp, DKp, bh, n, m, d, st, fz);
+                case 48: return launch_bwd_fast<T, 48, DQ, DK>(G, Q, K, DQp, DKp, bh, n, m, d, st, fz);
+                case 52: return launch_bwd_fast<T, 52, DQ, DK>(G, Q, K, DQp, DKp, bh, n, m, d, st, fz);
+                case 56: return launch_bwd_fast<T, 56, DQ, DK>(G, Q, K, DQp, DKp, bh, n, m, d, st, fz);
+                default: return launch_bwd_fast<T, 64, DQ, DK>(G, Q, K, DQp, DKp, bh, n, m, d, st, fz);
             }
         }
     }
@@ -1474,14 +1504,14 @@ int launch_bwd_t(const void* g, const void* q, const void* kT, void* dq, void* d
         if (DQ && DK && d <= 64 && m <= 256 && (m > 64 || d > 32)) {
             const int mc = m <= 64 ? 1 : (m <= 128 ? 2 : 4);
             if (d <= 32) {
-                if (mc == 2) return launch_bwd_wide<T, 1, 2>(G, Q, K, DQp, DKp, bh, n, m, d, st);
-                return launch_bwd_wide<T, 1, 4>(G, Q, K, DQp, DKp, bh, n, m, d, st);
+                if (mc == 2) return launch_bwd_wide<T, 1, 2>(G, Q, K, DQp, DKp, bh, n, m, d, st, fz);
+                return launch_bwd_wide<T, 1, 4>(G, Q, K, DQp, DKp, bh, n, m, d, st, fz);
             }
-            if (mc == 1) return launch_bwd_wide<T, 2, 1>(G, Q, K, DQp, DKp, bh, n, m, d, st);
-            if (mc == 2) return launch_bwd_wide<T, 2, 2>(G, Q, K, DQp, DKp, bh, n, m, d, st);
+            if (mc == 1) return launch_bwd_wide<T, 2, 1>(G, Q, K, DQp, DKp, bh, n, m, d, st, fz);
+            if (mc == 2) return launch_bwd_wide<T, 2, 2>(G, Q, K, DQp, DKp, bh, n, m, d, st, fz);
             // 128 < m <= 256: 32 landmarks per warp, 16 warps (half the
             // registers per thread of 64-landmark warps, twice the warps per SM)
-            return launch_bwd_wide<T, 2, 8, 32, 2 * kThreads>(G, Q, K, DQp, DKp, bh, n, m, d, st);
+            return launch_bwd_wide<T, 2, 8, 32, 2 * kThreads>(G, Q, K, DQp, DKp, bh, n, m, d, st, fz);
         }
     }
     int mcn = 1;
@@ -1493,7 +1523,7 @@ int launch_bwd_t(const void* g, const void* q, const void* kT, void* dq, void* d
     constexpr int kMinb = (DQ && sizeof(T) != 8) ? 2 : 1;
 #define LF_BWD_CASE(MBV)                                                                              \
     case MBV:                                                                                         \
-        return launch_bwd_mb<T, MBV, DQ, DK, kMinb>(G, Q, K, DQp, DKp, bh, n, m, d, mcn, st);
+        return launch_bwd_mb<T, MBV, DQ, DK, kMinb>(G, Q, K, DQp, DKp, bh, n, m, d, mcn, st, fz);
     switch (mb) {
         LF_BWD_CASE(8) LF_BWD_CASE(16) LF_BWD_CASE(24) LF_BWD_CASE(32) LF_BWD_CASE(40)
         LF_BWD_CASE(48) LF_BWD_CASE(52) LF_BWD_CASE(56) LF_BWD_CASE(64)
@@ -1630,7 +1660,7 @@ extern "C" int lf_laplace_kernel_fwd(const void* q, const void* kT, void* kmat, 
 }
 
 static int bwd_common(const void* g, const void* q, const void* kT, void* dq, void* dk, int64_t bh,
-                      int64_t n, int64_t m, int64_t d, int dtype, lf_stream_t stream) {
+                      int64_t n, int64_t m, int64_t d, int dtype, lf_stream_t stream, GFuse fz = {}) {
     int rc = check_args(g, q, kT, bh, n, m, d, dtype);
     if (rc) return rc;
     if (!dq && !dk) return LF_OK;
@@ -1642,9 +1672,9 @@ static int bwd_common(const void* g, const void* q, const void* kT, void* dq, vo
         if (dk && cudaMemsetAsync(dk, 0, (size_t)(bh * d * m) * es, st) != cudaSuccess) return check_launch("memset");
         return LF_OK;
     }
-    if (dq && dk) { LF_DISPATCH(dtype, T, return launch_bwd_t<T, true, true>(g, q, kT, dq, dk, bh, n, m, d, st)); }
-    if (dq) { LF_DISPATCH(dtype, T, return launch_bwd_t<T, true, false>(g, q, kT, dq, dk, bh, n, m, d, st)); }
-    LF_DISPATCH(dtype, T, return launch_bwd_t<T, false, true>(g, q, kT, dq, dk, bh, n, m, d, st));
+    if (dq && dk) { LF_DISPATCH(dtype, T, return launch_bwd_t<T, true, true>(g, q, kT, dq, dk, bh, n, m, d, st, fz)); }
+    if (dq) { LF_DISPATCH(dtype, T, return launch_bwd_t<T, true, false>(g, q, kT, dq, dk, bh, n, m, d, st, fz)); }
+    LF_DISPATCH(dtype, T, return launch_bwd_t<T, false, true>(g, q, kT, dq, dk, bh, n, m, d, st, fz));
     return LF_OK;
 }
 
@@ -1684,6 +1714,31 @@ extern "C" int lf_laplace_sub_bwd_ws(const void* g, const void* q, const void* k
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     LF_DISPATCH(dtype, T, return launch_bwd_flat_t<T>(g, q, kT, dq, dkT, bh, n, m, d, workspace, workspace_bytes,
                                                       nullptr, st));
+    return LF_OK;
+}
+
+// Gradients of Kmat = exp(scale * S) (lf_laplace_kernel_fwd) from dKmat, with
+// dS = scale * Kmat * dKmat formed while the backward stages its gradient
+// tile: no dS tensor is written or read.
+extern "C" int lf_laplace_kernel_bwd(const void* gk, const void* kmat, const void* q, const void* kT, void* dq,
+                                     void* dkT, int64_t bh, int64_t n, int64_t m, int64_t d, int dtype, double scale,
+                                     void* workspace, size_t workspace_bytes, lf_stream_t stream) {
+    clear_error();
+    if (!kmat && bh * n * m > 0) { set_error("null kmat"); return LF_ERR_INVALID; }
+    GFuse fz;
+    fz.km = kmat;
+    fz.kscale = (float)scale;
+    const size_t need = (dq && dkT && workspace) ? lf_laplace_sub_bwd_workspace_size(bh, n, m, d, dtype) : 0;
+    if (need == 0) return bwd_common(gk, q, kT, dq, dkT, bh, n, m, d, dtype, stream, fz);
+    int rc = check_args(gk, q, kT, bh, n, m, d, dtype);
+    if (rc) return rc;
+    if (reinterpret_cast<uintptr_t>(workspace) & 15) {
+        set_error("LaplaceKernel backward: workspace must be a 16-byte aligned device pointer");
+        return LF_ERR_INVALID;
+    }
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    LF_DISPATCH(dtype, T, return launch_bwd_flat_t<T>(gk, q, kT, dq, dkT, bh, n, m, d, workspace, workspace_bytes,
+                                                      nullptr, st, fz));
     return LF_OK;
 }
 

@@ -150,6 +150,32 @@ void LaplaceSubtraction_backward_cuda(const at::Tensor gradOutput, const at::Ten
              "LaplaceSubtraction_backward");
 }
 
+void LaplaceKernel_backward_cuda(const at::Tensor gradOutput, const at::Tensor output, double scale,
+                                 const at::Tensor query, const at::Tensor key, at::Tensor gradQuery,
+                                 at::Tensor gradKey) {
+    shape_check(query, key);
+    const std::vector<int64_t> sshape = {query.size(0), query.size(1), query.size(2), key.size(3)};
+    out_check(gradOutput.contiguous(), query, sshape, "gradOutput");
+    out_check(output, query, sshape, "output");
+    if (gradQuery.defined()) out_check(gradQuery, query, query.sizes(), "gradQuery");
+    if (gradKey.defined()) out_check(gradKey, query, key.sizes(), "gradKey");
+    c10::cuda::CUDAGuard guard(query.device());
+    at::Tensor g = gradOutput.contiguous();
+    Dims s = dims_of(query, key);
+    at::Tensor ws;
+    size_t need = 0;
+    if (gradQuery.defined() && gradKey.defined()) {
+        need = lf_laplace_sub_bwd_workspace_size(s.bh, s.n, s.m, s.d, dtype_code(query));
+        if (need) ws = at::empty({(int64_t)need}, query.options().dtype(at::kByte));
+    }
+    raise_on(lf_laplace_kernel_bwd(g.data_ptr(), output.data_ptr(), query.data_ptr(), key.data_ptr(),
+                                   gradQuery.defined() ? gradQuery.data_ptr() : nullptr,
+                                   gradKey.defined() ? gradKey.data_ptr() : nullptr, s.bh, s.n, s.m, s.d,
+                                   dtype_code(query), scale, need ? ws.data_ptr() : nullptr, need,
+                                   stream_of(query)),
+             "LaplaceKernel_backward");
+}
+
 void LaplaceSubtraction_reduce_forward_cuda(const at::Tensor query, const at::Tensor key, at::Tensor output) {
     shape_check(query, key);
     out_check(output, query, {query.size(0), query.size(1), query.size(2), key.size(3)}, "output");

@@ -63,6 +63,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.def("LaplaceKernel_forward", &LaplaceKernel_forward,
           "LaplaceKernel_forward (query, key, output, scale): output = exp(scale * LaplaceSub(query, key)), fused",
           py::arg("query"), py::arg("key"), py::arg("output"), py::arg("scale"));
+    m.def("LaplaceKernel_backward",
+          [](const at::Tensor& g, const at::Tensor& out, double scale, const at::Tensor& q, const at::Tensor& k,
+             c10::optional<at::Tensor> dq, c10::optional<at::Tensor> dk) {
+              LaplaceKernel_backward(g, out, scale, q, k, dq.has_value() ? *dq : at::Tensor(),
+                                     dk.has_value() ? *dk : at::Tensor());
+          },
+          "LaplaceKernel_backward (gradOutput, output, scale, query, key, gradQuery, gradKey): gradients of "
+          "output = exp(scale * LaplaceSub(query, key)); dS = scale * output * gradOutput is formed in the kernel",
+          py::arg("gradOutput"), py::arg("output"), py::arg("scale"), py::arg("query"), py::arg("key"),
+          py::arg("gradQuery"), py::arg("gradKey"));
     m.def("NewtonInverse_forward_ex", &NewtonInverse_forward_ex,
           "NewtonInverse_forward_ex (mat, output, iter, init_mode, reg, precision)", py::arg("mat"), py::arg("output"),
           py::arg("iter"), py::arg("init_mode") = 0, py::arg("reg") = 0.01, py::arg("precision") = 0);

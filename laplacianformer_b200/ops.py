@@ -67,7 +67,8 @@ def laplace_subtraction(query: torch.Tensor, key: torch.Tensor) -> torch.Tensor:
 
 class LaplaceKernelFn(torch.autograd.Function):
     """Kmat = exp(scale * LaplaceSub(Q, K^T)), forward fused into one kernel;
-    backward dS = scale * Kmat * dKmat, then the fused LaplaceSub backward."""
+    backward in one kernel too: dS = scale * Kmat * dKmat is formed while the
+    fused LaplaceSub backward stages its gradient tile (LaplaceKernel_backward)."""
 
     @staticmethod
     def forward(ctx, query, key, scale):
@@ -86,8 +87,7 @@ class LaplaceKernelFn(torch.autograd.Function):
         dq = torch.empty_like(query) if need_q else None
         dk = torch.empty_like(key) if need_k else None
         if need_q or need_k:
-            gs = (grad * out) * ctx.scale
-            ext().LaplaceSubtraction_backward(gs.contiguous(), query, key, dq, dk)
+            ext().LaplaceKernel_backward(grad.contiguous(), out, ctx.scale, query, key, dq, dk)
         return dq, dk, None
 
 
@@ -125,8 +125,8 @@ class LandmarkInverseFn(torch.autograd.Function):
     """X = NewtonInverse(exp(scale * LaplaceSub(L, L^T))) with A built inside
     the inverse kernel (lf_laplace_newton_inverse_fwd).  Backward:
     dA = -X^T G X^T (the inverse's analytic backward), dS = scale * A * dA with
-    A recomputed by the fused exp forward, then the LaplaceSub backward with L
-    as both query and key: dL = dQ + (dK^T)^T."""
+    A recomputed by the fused exp forward, then the LaplaceKernel backward
+    (dS formed inside it) with L as both query and key: dL = dQ + (dK^T)^T."""
 
     @staticmethod
     def forward(ctx, lmk, scale, iters, init_mode, reg, precision):
@@ -146,10 +146,9 @@ class LandmarkInverseFn(torch.autograd.Function):
         lT = lmk.transpose(-1, -2).contiguous()
         a = torch.empty_like(x)
         ext().LaplaceKernel_forward(lmk, lT, a, ctx.scale)
-        ds = (da * a) * ctx.scale
         dq = torch.empty_like(lmk)
         dkT = torch.empty_like(lT)
-        ext().LaplaceSubtraction_backward(ds.contiguous(), lmk, lT, dq, dkT)
+        ext().LaplaceKernel_backward(da, a, ctx.scale, lmk, lT, dq, dkT)  # dS = scale * A * dA in the kernel
         return dq + dkT.transpose(-1, -2), None, None, None, None, None
 
 

@@ -412,3 +412,46 @@ def test_laplace_kernel_autograd_matches_composition(cuda):
     (b * g).sum().backward()
     torch.testing.assert_close(q1.grad, q2.grad, rtol=1e-4, atol=1e-5)
     torch.testing.assert_close(k1.grad, k2.grad, rtol=1e-4, atol=1e-4)
+
+
+@pytest.mark.parametrize("shape", [(2, 2, 70, 32, 49), (1, 3, 33, 17, 5), (2, 1, 196, 64, 49), (1, 2, 49, 64, 196),
+                                   (1, 2, 300, 64, 256), (1, 1, 9, 100, 20)], ids=str)
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16], ids=str)
+def test_laplace_kernel_backward_fused(cuda, shape, dtype):
+    """dS = scale * Kmat * dKmat formed inside the backward kernel equals the
+    LaplaceSub backward of that dS (computed in fp32 from the same stored
+    values) within the backward tolerances, with and without workspace."""
+    q, k, g = _inputs(shape, dtype, seed=21)
+    qd, kd, gd = q.to(cuda), k.to(cuda), g.to(cuda)
+    scale = -1.0 / 64.0  # keeps Kmat and the gradients in the normal range of fp16
+    kmat = capi.laplace_kernel_fwd(qd, kd, scale)
+    ds32 = (gd.float() * kmat.float()) * scale
+    rq = np.asarray(O.laplace_bwd_query(ds32.cpu(), q.float(), k.float()), dtype=np.float64)
+    rk = np.asarray(O.laplace_bwd_key(ds32.cpu(), q.float(), k.float()), dtype=np.float64)
+    ga = np.abs(ds32.cpu().double().numpy())
+    row, col = ga.sum(-1, keepdims=True), ga.sum(-2)[:, :, None, :]
+    tol = _bwd_tol(dtype)
+    need = capi.laplace_sub_bwd_workspace_size(qd, kd)
+    ws = torch.full((max(need, 16) // 4,), float("nan"), device=cuda).view(torch.uint8) if need else None
+    for workspace in (None, ws):
+        dq, dk = capi.laplace_kernel_bwd(gd, kmat, qd, kd, scale, workspace=workspace)
+        torch.cuda.synchronize()
+        floor = {torch.float32: 1e-30, torch.float16: 2.0 ** -25, torch.bfloat16: 1e-30}[dtype]  # fp16 subnormal half-ulp
+        assert np.all(np.abs(_np(dq) - rq) <= tol * row + floor)
+        assert np.all(np.abs(_np(dk) - rk) <= tol * col + floor)
+
+
+def test_laplace_kernel_autograd_uses_fused_backward(cuda):
+    from laplacianformer_b200.ops import laplace_kernel
+
+    q, k, g = _inputs((2, 2, 50, 32, 13), torch.float32, seed=22)
+    qd = q.to(cuda).requires_grad_()
+    kd = k.to(cuda).requires_grad_()
+    out = laplace_kernel(qd, kd, -0.25)
+    out.backward(g.to(cuda))
+    q2 = q.double().requires_grad_()
+    k2 = k.double().requires_grad_()
+    ref = torch.exp(-0.25 * (q2[..., :, None, :] - k2.transpose(-1, -2)[..., None, :, :]).abs().sum(-1))
+    ref.backward(g.double())
+    torch.testing.assert_close(qd.grad.double().cpu(), q2.grad, rtol=0, atol=1e-5 * q2.grad.abs().max().item())
+    torch.testing.assert_close(kd.grad.double().cpu(), k2.grad, rtol=0, atol=1e-5 * k2.grad.abs().max().item())
