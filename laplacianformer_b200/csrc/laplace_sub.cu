@@ -72,6 +72,42 @@ int64_t cta_slots(K kern, size_t smem, int threads = kThreads) {
     return (int64_t)per_sm * num_sms();
 }
 
+// Clusters of `csize` CTAs (`threads` threads, `smem` bytes each) that the
+// current device runs at once (0: the size does not fit); cached like
+// cta_slots.
+template <typename K>
+int active_clusters(K kern, int csize, int threads, size_t smem) {
+    static std::mutex mu;
+    static std::map<std::tuple<const void*, int, size_t, int, int>, int> cache;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const auto key = std::make_tuple(reinterpret_cast<const void*>(kern), dev, smem, threads, csize);
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        auto it = cache.find(key);
+        if (it != cache.end()) return it->second;
+    }
+    cudaLaunchConfig_t probe = {};
+    probe.gridDim = dim3((unsigned)csize, 1, 1);
+    probe.blockDim = dim3((unsigned)threads, 1, 1);
+    probe.dynamicSmemBytes = smem;
+    cudaLaunchAttribute pa[1];
+    pa[0].id = cudaLaunchAttributeClusterDimension;
+    pa[0].val.clusterDim.x = (unsigned)csize;
+    pa[0].val.clusterDim.y = 1;
+    pa[0].val.clusterDim.z = 1;
+    probe.attrs = pa;
+    probe.numAttrs = 1;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, kern, &probe) != cudaSuccess) {
+        cudaGetLastError();
+        clusters = 0;
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    cache[key] = clusters;
+    return clusters;
+}
+
 // ---------------------------------------------------------------------------
 // Forward
 // ---------------------------------------------------------------------------
@@ -1181,8 +1217,10 @@ lsub_bwd_wide_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* 
     const int split = blockIdx.x;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int db = warp % DBT, mcb = (warp / DBT) % MCNT, rg = warp / (DBT * MCNT);
-    const int cl = db * 32 + lane, c = cl;
-    const bool lane_active = c < d;
+    const int cbase = (int)blockIdx.z * CW;  // channel group of this CTA (grid.z)
+    const int cw = min(CW, d - cbase);       // channels of the group
+    const int cl = db * 32 + lane, c = cbase + cl;
+    const bool lane_active = cl < cw;
     const int j0 = mcb * MB;
     const int sj = tid % MPT, srow0 = tid / MPT;    // staging column / first row
     constexpr int SRS = NT / MPT;             // staging row stride
@@ -1217,7 +1255,7 @@ lsub_bwd_wide_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* 
             const int e = tid + NT * k;
             const int i = e / CW, x = e % CW;
             const int64_t row = rc + i;
-            pq[k] = (row < r_end && x < d) ? Elem<T>::load(Qb[row * d + x]) : A(0);
+            pq[k] = (row < r_end && x < cw) ? Elem<T>::load(Qb[row * d + cbase + x]) : A(0);
         }
     };
     if (r_begin < r_end) load_chunk(r_begin);
@@ -1275,14 +1313,14 @@ lsub_bwd_wide_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* 
         // dQ = 2 * sum over landmark chunks (fixed order) - row sum of dS
         for (int e = tid; e < rows * CW; e += NT) {
             const int i = e / CW, x = e % CW;
-            if (x >= d) continue;
+            if (x >= cw) continue;
             A acc = A(0);
 #pragma unroll
             for (int b = 0; b < MCNT; ++b) acc += dqp[(b * RC + i) * CW + x];
             A rs = A(0);
 #pragma unroll
             for (int w = 0; w < WPR; ++w) rs += rpart[i * WPR + w];
-            dq[((int64_t)bh * n + rc + i) * d + x] = Elem<T>::store(A(2) * acc - rs);
+            dq[((int64_t)bh * n + rc + i) * d + cbase + x] = Elem<T>::store(A(2) * acc - rs);
         }
     }
 
@@ -1307,7 +1345,7 @@ lsub_bwd_wide_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* 
     __syncthreads();
     for (int e = tid; e < CW * m; e += NT) {
         const int cc = e / m, j = e % m;
-        if (cc >= d) continue;
+        if (cc >= cw) continue;
         A s = csum[j];
         if (RG == 1) {
             s += dkb[cc * KSTR + j];
@@ -1319,10 +1357,10 @@ lsub_bwd_wide_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* 
     cluster.sync();
     const int cs = (int)cluster.num_blocks();
     const int rank = (int)cluster.block_rank();
-    const int total = d * m;
+    const int total = cw * m;
     const int per = (total + cs - 1) / cs;
     const int e0 = rank * per, e1 = min(total, e0 + per);
-    T* dkout = dk + (int64_t)bh * d * m;
+    T* dkout = dk + ((int64_t)bh * d + cbase) * m;
     for (int e = e0 + tid; e < e1; e += NT) {
         const int cc = e / m, j = e - cc * m;
         A s = A(0);
@@ -1356,18 +1394,31 @@ int launch_bwd_wide(const T* g, const T* q, const T* kT, T* dq, T* dk, int64_t b
     if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     const int64_t slots = cta_slots(kern, smem, NT);
     const int64_t max_by_rows = (n + RC - 1) / RC;
+    (void)slots;
+    const int64_t groups = (d + CW - 1) / CW;  // channel groups over grid.z
+    // Cluster size: the CTAs of one (b,h) split its rows and form a cluster,
+    // so a cluster must fit in one GPC.  For each size the driver reports how
+    // many such clusters run at once; the estimated time is the number of
+    // waves times the rows per CTA.  Sizes above 8 (non-portable) help when
+    // there are few (b,h) per GPU (configuration 5 over 8 GPUs: 16).
+    int cmax = 8;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess) cmax = 16;
+    else cudaGetLastError();
     int64_t cs = 1;
-    double best = -1.0;
-    for (int64_t c = 1; c <= 8 && c <= (max_by_rows < 1 ? 1 : max_by_rows); ++c) {
-        double eff = wave_efficiency(bh * c, slots);
-        if (eff > best + 1e-9) { best = eff; cs = c; }
+    double best_t = -1.0;
+    for (int c = 1; c <= cmax && c <= (max_by_rows < 1 ? 1 : max_by_rows); ++c) {
+        const int clusters = active_clusters(kern, c, NT, smem);
+        if (clusters < 1) continue;
+        const double waves = (double)((bh * groups + clusters - 1) / clusters);
+        const double t = waves * (double)((n + c - 1) / c);
+        if (best_t < 0.0 || t < best_t * (1.0 - 1e-9)) { best_t = t; cs = c; }
     }
     int64_t rpc = (n + cs - 1) / cs;
     rpc = ((rpc + RC - 1) / RC) * RC;
     geo.rows_per_cta = (int)rpc;
     if (bh > 65535) { set_error("b*h = %lld exceeds 65535", (long long)bh); return LF_ERR_UNSUPPORTED; }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)cs, (unsigned)bh, 1);
+    cfg.gridDim = dim3((unsigned)cs, (unsigned)bh, (unsigned)groups);
     cfg.blockDim = dim3(NT, 1, 1);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
