@@ -463,8 +463,9 @@ def config5_record(args, rank, world, dev, n_tokens, gather, flush):
     dq, dk = torch.empty_like(q), torch.empty_like(kT)
     Lf = L.float().contiguous()
     LfT = Lf.transpose(-1, -2).contiguous()
-    sll = torch.empty(1, bh, M, M, device=dev)
-    X = torch.empty_like(sll)
+    A = torch.empty(1, bh, M, M, device=dev)
+    X = torch.empty_like(A)
+    ws = torch.empty(max(1, capi.laplace_sub_bwd_workspace_size(q, kT)), dtype=torch.uint8, device=dev)
     sigma = math.sqrt(D)
     chunk = -(-(B * H) // world)
     gbufs = None
@@ -477,9 +478,8 @@ def config5_record(args, rank, world, dev, n_tokens, gather, flush):
 
     def compute():
         capi.laplace_sub_fwd(q, kT, s)
-        capi.laplace_sub_bwd(ds, q, kT, dq, dk)
-        capi.laplace_sub_fwd(Lf, LfT, sll)
-        A = torch.exp(sll * (-1.0 / sigma))
+        capi.laplace_sub_bwd(ds, q, kT, dq, dk, workspace=ws)
+        capi.laplace_kernel_fwd(Lf, LfT, -1.0 / sigma, out=A)  # exp(-cdist_1 / sigma), S never stored
         capi.newton_inverse_fwd(A, 10, out=X)
 
     def gather_all():
@@ -500,7 +500,7 @@ def config5_record(args, rank, world, dev, n_tokens, gather, flush):
         g_ms = statistics.mean(time_steps(gather_all, steps, 3, flush, stream))
     ranks = per_rank([statistics.mean(times), g_ms])
     ms = max(r[0] for r in ranks)
-    launches = steps * (5 + (0 if gbufs is None else 3))  # our 4 kernels + the exp; NCCL gathers are NCCL's
+    launches = steps * 5  # fwd, bwd + its dK finalize, landmark kernel, inverse; NCCL gathers are NCCL's
     return {
         "value": B * H * N * M / (ms / 1e3) / 1e9, "unit": UNIT, "ms_per_step": ms, "steps": steps,
         "gather_ms": max(r[1] for r in ranks), "scaling": "strong", "dtype": "bf16 (inverse fp32)",

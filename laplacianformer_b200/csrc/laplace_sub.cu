@@ -1151,6 +1151,10 @@ int launch_bwd_flat(const T* g, const T* q, const T* kT, T* dq, T* dk, int64_t b
     return check_launch("lsub_bwd_dk_finalize");
 }
 
+template <typename T, int DBT, int MCNT, int MB, int NT>
+int launch_bwd_wide_flat(const T* g, const T* q, const T* kT, T* dq, T* dk, int64_t bh, int64_t n, int64_t m,
+                         int64_t d, float* ws, size_t ws_bytes, size_t* need, cudaStream_t st, GFuse fz = {});
+
 template <typename T>
 int launch_bwd_flat_t(const void* g, const void* q, const void* kT, void* dq, void* dk, int64_t bh, int64_t n,
                       int64_t m, int64_t d, void* ws, size_t ws_bytes, size_t* need, cudaStream_t st,
@@ -1159,13 +1163,17 @@ int launch_bwd_flat_t(const void* g, const void* q, const void* kT, void* dq, vo
     if constexpr (sizeof(T) == 8) {
         return LF_OK;
     } else {
-        if (!(d <= 32 && m <= 64)) return LF_OK;
         const T* G = static_cast<const T*>(g);
         const T* Q = static_cast<const T*>(q);
         const T* K = static_cast<const T*>(kT);
         T* DQp = static_cast<T*>(dq);
         T* DKp = static_cast<T*>(dk);
         float* W = static_cast<float*>(ws);
+        // configuration-5 channels and landmarks: the 16-warp wide kernel
+        if (d > 32 && d <= 64 && m > 128 && m <= 256)
+            return launch_bwd_wide_flat<T, 2, 8, 32, 2 * kThreads>(G, Q, K, DQp, DKp, bh, n, m, d, W, ws_bytes, need,
+                                                                    st, fz);
+        if (!(d <= 32 && m <= 64)) return LF_OK;
         const int64_t m4 = (m + 3) & ~3;
         switch (m4 <= 16 ? 16 : (m4 <= 32 ? 32 : (m4 <= 48 ? 48 : (m4 <= 52 ? 52 : (m4 <= 56 ? 56 : 64))))) {
             case 16: return launch_bwd_flat<T, 16>(G, Q, K, DQp, DKp, bh, n, m, d, W, ws_bytes, need, st, fz);
@@ -1188,10 +1196,10 @@ int launch_bwd_flat_t(const void* g, const void* q, const void* kT, void* dq, vo
 // landmark chunks and dK partials of the row groups are combined in a fixed
 // order (bitwise reproducible); the row-split CTAs of one (b,h) form a
 // cluster and add their dK through distributed shared memory.
-template <typename T, int DBT, int MCNT, int MB, int NT>
+template <typename T, int DBT, int MCNT, int MB, int NT, bool FLAT>
 __global__ void __launch_bounds__(NT, 1)
 lsub_bwd_wide_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* __restrict__ kT,
-                     T* __restrict__ dq, T* __restrict__ dk, BwdGeom geo) {
+                     T* __restrict__ dq, T* __restrict__ dk, BwdGeom geo, float* __restrict__ ws) {
     using A = typename Elem<T>::acc;
     constexpr int MPT = MB * MCNT;             // padded landmarks
     constexpr int CW = 32 * DBT;               // channels per CTA
@@ -1212,9 +1220,6 @@ lsub_bwd_wide_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* 
     A* dkb = dqp + MCNT * RC * CW;                  // [CW][KSTR]
     A* dpart = dkb + CW * KSTR;                     // [RG][CW][KSTR] (RG > 1)
 
-    cg::cluster_group cluster = cg::this_cluster();
-    const int bh = blockIdx.y;
-    const int split = blockIdx.x;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int db = warp % DBT, mcb = (warp / DBT) % MCNT, rg = warp / (DBT * MCNT);
     const int cbase = (int)blockIdx.z * CW;  // channel group of this CTA (grid.z)
@@ -1225,6 +1230,27 @@ lsub_bwd_wide_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* 
     const int sj = tid % MPT, srow0 = tid / MPT;    // staging column / first row
     constexpr int SRS = NT / MPT;             // staging row stride
 
+    // FLAT: this CTA walks a contiguous run of P 64-row units of the flattened
+    // (b,h) x rows space, one segment per (b,h) it touches; otherwise one
+    // segment: rows [x * rows_per_cta, ...) of (b,h) = blockIdx.y.
+    int64_t u = FLAT ? (int64_t)blockIdx.x * geo.P : 0;
+    const int64_t u_end = FLAT ? ((u + geo.P < geo.total) ? u + geo.P : geo.total) : 1;
+    for (int seg = 0; u < u_end; ++seg) {
+    int bh;
+    int64_t r_begin, r_end, u_next;
+    if constexpr (FLAT) {
+        bh = (int)(u / geo.U);
+        const int64_t ub = (int64_t)bh * geo.U;
+        u_next = (ub + geo.U < u_end) ? ub + geo.U : u_end;
+        r_begin = (u - ub) * kRowChunk;
+        r_end = (u_next - ub) * kRowChunk;
+        if (r_end > n) r_end = n;
+    } else {
+        bh = blockIdx.y;
+        r_begin = (int64_t)blockIdx.x * geo.rows_per_cta;
+        r_end = (r_begin + geo.rows_per_cta < (int64_t)n) ? r_begin + geo.rows_per_cta : (int64_t)n;
+        u_next = 1;
+    }
     const T* Gb = g + (int64_t)bh * n * m;
     const T* Qb = q + (int64_t)bh * n * d;
     const T* Kb = kT + (int64_t)bh * d * m;
@@ -1238,8 +1264,6 @@ lsub_bwd_wide_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* 
     }
     A colacc = A(0);
 
-    const int64_t r_begin = (int64_t)split * geo.rows_per_cta;
-    const int64_t r_end = (r_begin + geo.rows_per_cta < (int64_t)n) ? r_begin + geo.rows_per_cta : (int64_t)n;
 
     A pg[GPT], pq[QPT];
     auto load_chunk = [&](int64_t rc) {
@@ -1354,6 +1378,23 @@ lsub_bwd_wide_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* 
         }
         dkb[cc * KSTR + j] = s;
     }
+    if constexpr (FLAT) {
+        // A (b,h) wholly inside this CTA gets its dK^T directly; the part of a
+        // (b,h) shared with other CTAs goes to slot 2*CTA (first segment) or
+        // 2*CTA+1 (last), summed in CTA order by lsub_bwd_dk_finalize.
+        const bool whole = (u == (int64_t)bh * geo.U) && (u_next == (int64_t)bh * geo.U + geo.U);
+        T* dkout = dk + ((int64_t)bh * d + cbase) * m;
+        float* slot = ws + ((int64_t)2 * blockIdx.x + (seg == 0 ? 0 : 1)) * d * m + (int64_t)cbase * m;
+        for (int e = tid; e < cw * m; e += NT) {
+            const int cc = e / m, j = e - cc * m;
+            const A v = dkb[cc * KSTR + j];
+            if (whole) dkout[e] = Elem<T>::store(v);
+            else slot[e] = (float)v;
+        }
+        __syncthreads();  // the shared buffers are reused by the next segment
+        u = u_next;
+    } else {
+    cg::cluster_group cluster = cg::this_cluster();
     cluster.sync();
     const int cs = (int)cluster.num_blocks();
     const int rank = (int)cluster.block_rank();
@@ -1371,6 +1412,9 @@ lsub_bwd_wide_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* 
         dkout[e] = Elem<T>::store(s);
     }
     cluster.sync();
+    u = u_next;
+    }
+    }  // segments
 }
 
 template <typename T, int DBT, int MCNT, int MB = 64, int NT = kThreads>
@@ -1390,7 +1434,7 @@ int launch_bwd_wide(const T* g, const T* q, const T* kT, T* dq, T* dk, int64_t b
         set_error("LaplaceSubtraction backward: needs %zu bytes of shared memory", smem);
         return LF_ERR_UNSUPPORTED;
     }
-    auto kern = lsub_bwd_wide_kernel<T, DBT, MCNT, MB, NT>;
+    auto kern = lsub_bwd_wide_kernel<T, DBT, MCNT, MB, NT, false>;
     if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     const int64_t slots = cta_slots(kern, smem, NT);
     const int64_t max_by_rows = (n + RC - 1) / RC;
@@ -1429,12 +1473,57 @@ int launch_bwd_wide(const T* g, const T* q, const T* kT, T* dq, T* dk, int64_t b
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaError_t err = cudaLaunchKernelEx(&cfg, kern, g, q, kT, dq, dk, geo);
+    cudaError_t err = cudaLaunchKernelEx(&cfg, kern, g, q, kT, dq, dk, geo, static_cast<float*>(nullptr));
     if (err != cudaSuccess) {
         set_error("lsub_bwd_wide_kernel launch: %s", cudaGetErrorString(err));
         return LF_ERR_CUDA;
     }
     return check_launch("lsub_bwd_wide_kernel");
+}
+
+// Balanced launch of the wide backward (both gradients, workspace): every CTA
+// slot of the GPU takes a contiguous run of P 64-row units of all (b,h)
+// (lf_laplace_sub_bwd_ws), as for the fast kernel; the dKT partials of a
+// (b,h) shared by several CTAs are summed by lsub_bwd_dk_finalize.
+template <typename T, int DBT, int MCNT, int MB, int NT>
+int launch_bwd_wide_flat(const T* g, const T* q, const T* kT, T* dq, T* dk, int64_t bh, int64_t n, int64_t m,
+                         int64_t d, float* ws, size_t ws_bytes, size_t* need, cudaStream_t st, GFuse fz) {
+    using A = typename Elem<T>::acc;
+    constexpr int MPT = MB * MCNT, CW = 32 * DBT, RG = (NT / 32) / (DBT * MCNT), RC = 4096 / MPT;
+    BwdGeom geo;
+    geo.n = (int)n; geo.m = (int)m; geo.d = (int)d;
+    geo.km = fz.km; geo.kscale = fz.kscale;
+    geo.DBC = DBT; geo.MCN = MCNT; geo.RG = RG; geo.MP = MPT; geo.RC = RC;
+    geo.KSTR = (int)(m | 1);
+    geo.rows_per_cta = 0;
+    size_t smem = sizeof(A) * ((size_t)RC * MPT + (size_t)RC * CW + (size_t)RC * (MPT / 32) + MPT +
+                               (size_t)(NT / MPT) * MPT + (size_t)MCNT * RC * CW + (size_t)CW * geo.KSTR +
+                               (RG > 1 ? (size_t)RG * CW * geo.KSTR : 0));
+    if (smem > (size_t)max_optin_smem()) {
+        set_error("LaplaceSubtraction backward: needs %zu bytes of shared memory", smem);
+        return LF_ERR_UNSUPPORTED;
+    }
+    auto kern = lsub_bwd_wide_kernel<T, DBT, MCNT, MB, NT, true>;
+    if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    const int64_t slots = cta_slots(kern, smem, NT);
+    geo.U = (n + kRowChunk - 1) / kRowChunk;
+    geo.total = bh * geo.U;
+    geo.P = (geo.total + slots - 1) / slots;
+    const int64_t grid = (geo.total + geo.P - 1) / geo.P;
+    const size_t bytes = (size_t)2 * grid * d * m * sizeof(float);
+    if (need) *need = bytes;
+    if (!ws) return LF_OK;
+    if (ws_bytes < bytes) {
+        set_error("LaplaceSubtraction backward: workspace of %zu bytes, %zu needed", ws_bytes, bytes);
+        return LF_ERR_INVALID;
+    }
+    kern<<<(unsigned)grid, NT, smem, st>>>(g, q, kT, dq, dk, geo, ws);
+    int rc = check_launch("lsub_bwd_wide_kernel");
+    if (rc) return rc;
+    if (bh > 0x7fffffff) { set_error("b*h too large"); return LF_ERR_UNSUPPORTED; }
+    const unsigned eblocks = (unsigned)((d * m + kThreads - 1) / kThreads);
+    lsub_bwd_dk_finalize<T><<<dim3((unsigned)bh, eblocks, 1), kThreads, 0, st>>>(ws, dk, (int)d, (int)m, geo.U, geo.P);
+    return check_launch("lsub_bwd_dk_finalize");
 }
 
 // Landmark chunk per warp (MB) and number of chunks (mcn): least padding of m

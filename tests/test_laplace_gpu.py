@@ -338,6 +338,8 @@ def _bwd_plain(g, q, k):
     (50, 3, 1, 32, 49),     # single query row
     (1, 1, 3000, 32, 64),   # one (b,h) split over many CTAs
     (4, 2, 3136, 32, 49),   # configuration-2 rows
+    (3, 2, 700, 64, 256),   # configuration-5 channels / landmarks (16-warp wide kernel, balanced)
+    (1, 3, 1000, 40, 131),  # ragged, same kernel
 ], ids=str)
 @pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16], ids=str)
 def test_balanced_backward_matches_oracle_and_cluster_kernel(cuda, shape, dtype):
