@@ -22,8 +22,10 @@ Sub-records of the same line:
   NewtonInverse_forward (reference init, A + 0.01 I, split3);
 * ``config5`` — the north-star long-sequence workload (B=8, H=16, N=16384,
   D=64, M=256, bf16 LaplaceSub fwd+bwd + the 256x256 landmark inverse x10)
-  strong-scaled over the ranks, with dQ, dK^T and X all-gathered over NCCL
-  after the compute when N > 1;
+  strong-scaled over the ranks; with N > 1 dQ, dK^T and X are replicated on
+  every rank by the kernels' own stores into the other GPUs' gather buffers
+  (NVLink peer memory), with the NCCL all-gather after the compute timed
+  beside it;
 * ``config4`` — the Laplacian attention block fwd+bwd, bf16 [128,8,196,64],
   M = 49, 8 iterations (rank 0 of a 1-GPU run).
 
@@ -425,7 +427,7 @@ def run_b200(args, rank, world, dev):
         line["newton_inverse"] = newton_section(dev, args.steps, args.warmup, flush, stream, peaks, peak_kind)
         line["gpu_launches"] += 3 * max(2, args.steps // 2)
     if not args.skip_config5:
-        c5 = config5_record(args, rank, world, dev, args.n_tokens, "after" if world > 1 else "none", flush)
+        c5 = config5_record(args, rank, world, dev, args.n_tokens, args.gather if world > 1 else "none", flush)
         line["config5"] = c5
         line["gpu_launches"] += c5.pop("launches")
     if world == 1 and not args.skip_config4:
@@ -441,9 +443,14 @@ def run_b200(args, rank, world, dev):
 def config5_record(args, rank, world, dev, n_tokens, gather, flush):
     """Configuration 5: B=8, H=16, D=64, M=256 chunk-mean landmarks, bf16 Q/K,
     LaplaceSub fwd+bwd plus the 256x256 landmark-kernel inverse (fp32, 10
-    iterations).  Strong scaling: the 128 (b,h) slices are split over ranks;
-    with gather "after", dQ, dK^T and X are all-gathered over NCCL after the
-    compute (S stays sharded), and the gather is timed on its own as well."""
+    iterations).  Strong scaling: the 128 (b,h) slices are split over ranks,
+    and dQ, dK^T and X end up replicated on every rank (S stays sharded:
+    gathering it would move more bytes over NVLink than the sharded compute
+    saves).  gather "peer": the backward stores every dQ tile into all ranks'
+    IPC-mapped gather buffers as it computes it, dK^T and X are pushed by a
+    put kernel, and a stream-ordered flag barrier ends the step; gather
+    "after": the same outputs all-gathered over NCCL after the compute (also
+    timed beside "peer" as the collective baseline, with the gather alone)."""
     from laplacianformer_b200 import capi, workloads
     from laplacianformer_b200.sharding import shard_bounds
 
@@ -460,58 +467,103 @@ def config5_record(args, rank, world, dev, n_tokens, gather, flush):
     ds = torch.randn(1, bh, N, M, generator=g, device=dev).to(torch.bfloat16)
     del k
     s = torch.empty(1, bh, N, M, device=dev, dtype=torch.bfloat16)
-    dq, dk = torch.empty_like(q), torch.empty_like(kT)
     Lf = L.float().contiguous()
     LfT = Lf.transpose(-1, -2).contiguous()
     A = torch.empty(1, bh, M, M, device=dev)
-    X = torch.empty_like(A)
     ws = torch.empty(max(1, capi.laplace_sub_bwd_workspace_size(q, kT)), dtype=torch.uint8, device=dev)
     sigma = math.sqrt(D)
     chunk = -(-(B * H) // world)
-    gbufs = None
-    if gather == "after":
-        # replicated dQ, dK^T and X on every rank (S stays sharded: gathering
-        # it would move more bytes over NVLink than the sharded compute saves)
+    steps = max(3, min(args.steps, 10))
+
+    def compute(dq, dk, X, dq_peers=None):
+        capi.laplace_sub_fwd(q, kT, s)
+        if dq_peers:
+            capi.laplace_sub_bwd_peers(ds, q, kT, dq, dk, dq_peers, workspace=ws)
+        else:
+            capi.laplace_sub_bwd(ds, q, kT, dq, dk, workspace=ws)
+        capi.laplace_kernel_fwd(Lf, LfT, -1.0 / sigma, out=A)  # exp(-cdist_1 / sigma), S never stored
+        capi.newton_inverse_fwd(A, 10, out=X)
+
+    dq, dk = torch.empty_like(q), torch.empty_like(kT)
+    X = torch.empty_like(A)
+    rec = {}
+    if gather in ("after", "peer"):
+        # NCCL baseline: replicated dQ, dK^T and X through all_gather_into_tensor
         gbufs = [torch.empty((world * chunk,) + tuple(t.shape[2:]), device=dev, dtype=t.dtype) for t in (dq, dk, X)]
         sends = [t[0] if bh == chunk else torch.zeros((chunk,) + tuple(t.shape[2:]), device=dev, dtype=t.dtype)
                  for t in (dq, dk, X)]
 
-    def compute():
-        capi.laplace_sub_fwd(q, kT, s)
-        capi.laplace_sub_bwd(ds, q, kT, dq, dk, workspace=ws)
-        capi.laplace_kernel_fwd(Lf, LfT, -1.0 / sigma, out=A)  # exp(-cdist_1 / sigma), S never stored
-        capi.newton_inverse_fwd(A, 10, out=X)
+        def gather_all():
+            for i, (t, buf) in enumerate(zip((dq, dk, X), gbufs)):
+                if bh != chunk:
+                    sends[i][:bh].copy_(t[0])
+                torch.distributed.all_gather_into_tensor(buf, sends[i] if bh != chunk else t[0])
 
-    def gather_all():
-        for i, (t, buf) in enumerate(zip((dq, dk, X), gbufs)):
-            if bh != chunk:
-                sends[i][:bh].copy_(t[0])
-            torch.distributed.all_gather_into_tensor(buf, sends[i] if bh != chunk else t[0])
-
-    def step():
-        compute()
-        if gbufs is not None:
+        def step_after():
+            compute(dq, dk, X)
             gather_all()
 
-    steps = max(3, min(args.steps, 10))
-    times = time_steps(step, steps, max(3, args.warmup), flush, stream)
-    g_ms = 0.0
-    if gbufs is not None:
-        g_ms = statistics.mean(time_steps(gather_all, steps, 3, flush, stream))
-    ranks = per_rank([statistics.mean(times), g_ms])
+        t_after = statistics.mean(time_steps(step_after, steps, max(3, args.warmup), flush, stream))
+        t_gather = statistics.mean(time_steps(gather_all, steps, 3, flush, stream))
+        del gbufs, sends
+        rec["nccl_after"] = [t_after, t_gather]
+    if gather == "peer":
+        from laplacianformer_b200.peer import PeerGather
+
+        try:
+            pg = PeerGather([((N, D), q.dtype), ((D, M), kT.dtype), ((M, M), torch.float32)], B * H, device=dev)
+        except RuntimeError as exc:  # every rank raises together; report the NCCL variant instead
+            rec["peer_error"] = str(exc)[:300]
+            gather = "after"
+    if gather == "peer":
+        pdq, pdk, pX = (pg.local(i)[:bh].unsqueeze(0) for i in range(3))
+        peers = [pg.peer_ptrs(i) for i in range(3)]
+
+        def step():
+            compute(pdq, pdk, pX, peers[0])
+            capi.peer_put(pdk[0], peers[1])
+            capi.peer_put(pX[0], peers[2])
+            pg.barrier(stream)
+
+        times = time_steps(step, steps, max(3, args.warmup), flush, stream)
+        torch.cuda.synchronize(dev)
+        status = capi.device_status(clear=True)
+        if status != capi.LF_OK:
+            raise RuntimeError(f"peer gather: device status {status} (a barrier wait expired)")
+        pg.close()
+        launches = steps * 8  # fwd, bwd + its dK finalize, landmark kernel, inverse, 2 puts, barrier
+        parallelism = ("dQ stored into every rank's IPC-mapped gather buffer by the backward kernel itself, "
+                       "dK^T/X pushed by a put kernel, flag barrier (no collective)")
+    elif gather == "after":
+        times = time_steps(step_after, steps, max(3, args.warmup), flush, stream) if "nccl_after" not in rec \
+            else [rec["nccl_after"][0]] * steps
+        launches = steps * 5  # NCCL's gathers are not ours
+        parallelism = "dQ/dK^T/X all_gather_into_tensor over NCCL after the compute"
+    else:
+        times = time_steps(lambda: compute(dq, dk, X), steps, max(3, args.warmup), flush, stream)
+        launches = steps * 5  # fwd, bwd + its dK finalize, landmark kernel, inverse
+        parallelism = "no collective"
+    after = rec.get("nccl_after", [0.0, 0.0])
+    ranks = per_rank([statistics.mean(times), after[0], after[1]])
     ms = max(r[0] for r in ranks)
-    launches = steps * 5  # fwd, bwd + its dK finalize, landmark kernel, inverse; NCCL gathers are NCCL's
-    return {
+    out = {
         "value": B * H * N * M / (ms / 1e3) / 1e9, "unit": UNIT, "ms_per_step": ms, "steps": steps,
-        "gather_ms": max(r[1] for r in ranks), "scaling": "strong", "dtype": "bf16 (inverse fp32)",
+        "scaling": "strong", "dtype": "bf16 (inverse fp32)",
         "workload": f"config5 N={N}: LaplaceSub fwd+bwd bf16 (B*H=128, M=256, D=64) + NewtonInverse 256x256 fp32 x10",
-        "parallelism": f"bh-shard x{world} (strong), " + ("no collective" if gbufs is None else
-                                                          "dQ/dK^T/X all_gather_into_tensor over NCCL after the compute"),
+        "parallelism": f"bh-shard x{world} (strong), " + parallelism,
         "newton_matrices_per_s": B * H / (ms / 1e3),
-        "per_rank": {"fields": ["step_ms", "gather_ms"], "values": ranks},
+        "per_rank": {"fields": ["step_ms", "nccl_after_step_ms", "nccl_gather_only_ms"], "values": ranks},
         "l2": "inputs larger than L2" if N >= 16384 else "flushed between timed steps",
         "launches": launches,
     }
+    if "peer_error" in rec:
+        out["peer_error"] = rec["peer_error"]
+    if "nccl_after" in rec:
+        out["nccl_after_step_ms"] = max(r[1] for r in ranks)
+        out["gather_ms"] = max(r[2] for r in ranks)
+    else:
+        out["gather_ms"] = 0.0
+    return out
 
 
 def config4_record(args, dev, flush, stream):
@@ -554,6 +606,7 @@ def run_config5(args, rank, world, dev):
         "config": {"workload": rec["workload"], "global_batch": 8, "heads": 16, "seq_len": args.n_tokens,
                    "parallelism": rec["parallelism"], "l2": rec["l2"]},
         "gather_ms": rec["gather_ms"], "per_rank": rec["per_rank"],
+        **{k: rec[k] for k in ("nccl_after_step_ms", "peer_error") if k in rec},
         "newton_matrices_per_s": rec["newton_matrices_per_s"], "gpu_launches": launches, "clocks": clk.summary(),
     }
 
@@ -683,8 +736,9 @@ def main():
     ap.add_argument("--ns-batch", type=int, default=4096)
     ap.add_argument("--workload", choices=["config2", "config5"], default="config2")
     ap.add_argument("--n-tokens", type=int, default=16384, help="configuration-5 sequence length")
-    ap.add_argument("--gather", choices=["none", "after"], default="after",
-                    help="--workload config5 with N>1: all-gather dQ, dK^T and X after the compute (or not at all)")
+    ap.add_argument("--gather", choices=["none", "after", "peer"], default="peer",
+                    help="config 5 with N>1: replicate dQ, dK^T and X on every rank by peer stores from the kernels "
+                         "(peer; the NCCL variant is timed beside it), by NCCL after the compute (after), or not at all")
     ap.add_argument("--skip-config5", action="store_true", help="leave the configuration-5 sub-record out")
     ap.add_argument("--skip-config4", action="store_true", help="leave the configuration-4 sub-record out")
     ap.add_argument("--no-cpu-baseline", action="store_true")

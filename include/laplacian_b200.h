@@ -54,6 +54,11 @@ enum lf_status {
     LF_ERR_TIMEOUT = 5       /* a device-side bounded wait expired           */
 };
 
+/* Remote destinations of the peer (NVLink) entry points: a node's other
+   GPUs, and the bytes of a peer-buffer handle (a CUDA IPC handle). */
+#define LF_MAX_PEERS 8
+#define LF_PEER_HANDLE_BYTES 64
+
 /* NewtonInverse initialisation modes. */
 enum lf_ns_init {
     /* P = A + reg*I, V0 = 1.8 / (max_i sum_j P_ij)^2 * P
@@ -281,6 +286,54 @@ LF_API int lf_device_status(int clear);
    error path the tensor-core kernels take instead of hanging.  No
    counterpart in the reference. */
 LF_API int lf_selftest_bounded_wait(int timeout_ms, lf_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+   Gather of a (b,h)-sharded run over NVLink peer memory.  The reference has no
+   multi-GPU code; its callers shard B*H over ranks and all-gather dQ, dK^T
+   and X with a collective afterwards.  These entry points let the producing
+   kernels write every rank's copy directly, one process per GPU.
+   ------------------------------------------------------------------------- */
+
+/* cudaMalloc(bytes), zeroed, and its IPC handle (LF_PEER_HANDLE_BYTES bytes
+   written to `handle`) for the other ranks to map with lf_peer_open.
+   Synchronous; free with lf_peer_free. */
+LF_API int lf_peer_alloc(size_t bytes, void** ptr, void* handle);
+
+/* Maps another process's lf_peer_alloc buffer (same node) into this device's
+   address space; unmap with lf_peer_close.  Synchronous. */
+LF_API int lf_peer_open(const void* handle, void** ptr);
+LF_API int lf_peer_close(void* ptr);
+LF_API int lf_peer_free(void* ptr);
+
+/* Copies `bytes` from local device memory `src` to each of the `ndst`
+   (<= LF_MAX_PEERS) destinations (local or peer device pointers). */
+LF_API int lf_peer_put(const void* src, size_t bytes, void* const* dsts, int ndst, lf_stream_t stream);
+
+/* Stream-ordered barrier of `world` ranks (<= LF_MAX_PEERS + 1):
+   flags[r] is rank r's uint32 flag array of `world` entries (an lf_peer_alloc
+   buffer, mapped here with lf_peer_open; flags[rank] is this rank's own).
+   Writes `epoch` into flags[r][rank] of every peer r with a system-scope
+   release after all earlier work on the stream, then waits until
+   flags[rank][r] has reached `epoch` for every peer r (so every peer's
+   earlier stores into this GPU are visible to later work on the stream).
+   Epochs must increase by one per call.  A wait longer than timeout_ms
+   (1..60000) gives up and records LF_ERR_TIMEOUT in the device status word
+   (lf_device_status). */
+LF_API int lf_peer_barrier(uint32_t* const* flags, int world, int rank, uint32_t epoch, int timeout_ms,
+                           lf_stream_t stream);
+
+/* lf_laplace_sub_bwd_ws that also stores dQ at the same element offsets into
+   each of the `npeer` (<= LF_MAX_PEERS) buffers dq_peers[i] (peer device
+   pointers from lf_peer_open, already offset to this rank's slice), so the
+   all-gather of dQ overlaps the backward.  Shapes the balanced wide kernel
+   (d <= 64, 128 < m <= 256) runs store from inside the kernel; other shapes
+   run lf_laplace_sub_bwd_ws and then lf_peer_put.  dK^T is written locally
+   only (push it with lf_peer_put).  Finish with lf_peer_barrier before a
+   peer reads its buffer. */
+LF_API int lf_laplace_sub_bwd_peers(const void* g, const void* q, const void* kT,
+                                    void* dq, void* dkT, void* const* dq_peers, int npeer,
+                                    int64_t bh, int64_t n, int64_t m, int64_t d, int dtype,
+                                    void* workspace, size_t workspace_bytes, lf_stream_t stream);
 
 #ifdef __cplusplus
 }

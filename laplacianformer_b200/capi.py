@@ -53,7 +53,18 @@ SIGNATURES = {
     "lf_newton_inverse_residual": (_I, [_P, _P, _P, _I64, _I64, _D, _I, _P]),
     "lf_device_status": (_I, [_I]),
     "lf_selftest_bounded_wait": (_I, [_I, _P]),
+    "lf_peer_alloc": (_I, [ctypes.c_size_t, ctypes.POINTER(_P), _P]),
+    "lf_peer_open": (_I, [_P, ctypes.POINTER(_P)]),
+    "lf_peer_close": (_I, [_P]),
+    "lf_peer_free": (_I, [_P]),
+    "lf_peer_put": (_I, [_P, ctypes.c_size_t, _P, _I, _P]),
+    "lf_peer_barrier": (_I, [_P, _I, _I, ctypes.c_uint32, _I, _P]),
+    "lf_laplace_sub_bwd_peers": (_I, [_P, _P, _P, _P, _P, _P, _I, _I64, _I64, _I64, _I64, _I, _P, ctypes.c_size_t,
+                                      _P]),
 }
+
+LF_MAX_PEERS = 8
+LF_PEER_HANDLE_BYTES = 64
 
 _lib = None
 
@@ -182,6 +193,40 @@ def laplace_sub_bwd(g, q, kT, dq=True, dk=True, workspace=None):
     _check(lib().lf_laplace_sub_bwd(_ptr(g), _ptr(q), _ptr(kT), _ptr(dq), _ptr(dk), bh, n, m, d, dtype_code(q),
                                     _stream(q)), "lf_laplace_sub_bwd")
     return dq, dk
+
+
+def _ptr_table(ptrs):
+    """A C array of device pointers (void* const*) kept alive by the caller."""
+    return (_P * max(1, len(ptrs)))(*[int(p) for p in ptrs])
+
+
+def laplace_sub_bwd_peers(g, q, kT, dq, dk, dq_peers, workspace=None):
+    """laplace_sub_bwd that also stores dQ into each peer pointer of
+    `dq_peers` (same layout as dq, e.g. PeerGather.peer_ptrs); both
+    gradients are required."""
+    _need_cuda(g, q, kT, dq, dk)
+    bh, n, m, d = _dims(q, kT)
+    if len(dq_peers) > LF_MAX_PEERS:
+        raise ValueError(f"at most {LF_MAX_PEERS} peers")
+    need = laplace_sub_bwd_workspace_size(q, kT)
+    if need and workspace is None:
+        workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+    ws_ptr, ws_bytes = (None, 0) if workspace is None else (_ptr(workspace), workspace.numel() * workspace.element_size())
+    table = _ptr_table(dq_peers)
+    _check(lib().lf_laplace_sub_bwd_peers(_ptr(g), _ptr(q), _ptr(kT), _ptr(dq), _ptr(dk), table, len(dq_peers),
+                                          bh, n, m, d, dtype_code(q), ws_ptr, ws_bytes, _stream(q)),
+           "lf_laplace_sub_bwd_peers")
+    return dq, dk
+
+
+def peer_put(src, dst_ptrs, stream=None):
+    """Copies the bytes of the contiguous device tensor `src` to every pointer of `dst_ptrs`."""
+    _need_cuda(src)
+    if not src.is_contiguous():
+        raise ValueError("peer_put needs a contiguous tensor")
+    st = _stream(src) if stream is None else stream.cuda_stream
+    table = _ptr_table(dst_ptrs)
+    _check(lib().lf_peer_put(_ptr(src), src.numel() * src.element_size(), table, len(dst_ptrs), st), "lf_peer_put")
 
 
 def laplace_sub_bwd_query(g, q, kT, out=None):

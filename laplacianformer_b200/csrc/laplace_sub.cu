@@ -594,13 +594,24 @@ struct BwdGeom {
     // S), same layout as dS) as they load it.
     const void* km = nullptr;
     float kscale = 0.f;
+    // Extra dQ destinations (peer GPUs' gather buffers, same element offsets),
+    // stored by the wide kernel beside dq (lf_laplace_sub_bwd_peers).
+    void* dqx[LF_MAX_PEERS] = {};
+    int ndqx = 0;
 };
 
-// The optional dS factor of the Laplacian-kernel backward (see BwdGeom::km).
+// The optional dS factor of the Laplacian-kernel backward (see BwdGeom::km)
+// and the extra dQ destinations of the wide kernel (see BwdGeom::dqx).
 struct GFuse {
     const void* km = nullptr;
     float kscale = 0.f;
+    void* const* dqx = nullptr;
+    int ndqx = 0;
 };
+
+// Shapes the balanced wide backward runs (configuration-5 channels and
+// landmarks); the others use the fast kernel or no workspace.
+inline bool wide_flat_shape(int64_t m, int64_t d) { return d > 32 && d <= 64 && m > 128 && m <= 256; }
 
 // dS value at index e of the (b,h) slice: g[e], or kscale * km[e] * g[e].
 template <typename T>
@@ -1170,7 +1181,7 @@ int launch_bwd_flat_t(const void* g, const void* q, const void* kT, void* dq, vo
         T* DKp = static_cast<T*>(dk);
         float* W = static_cast<float*>(ws);
         // configuration-5 channels and landmarks: the 16-warp wide kernel
-        if (d > 32 && d <= 64 && m > 128 && m <= 256)
+        if (wide_flat_shape(m, d))
             return launch_bwd_wide_flat<T, 2, 8, 32, 2 * kThreads>(G, Q, K, DQp, DKp, bh, n, m, d, W, ws_bytes, need,
                                                                     st, fz);
         if (!(d <= 32 && m <= 64)) return LF_OK;
@@ -1344,7 +1355,10 @@ lsub_bwd_wide_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* 
             A rs = A(0);
 #pragma unroll
             for (int w = 0; w < WPR; ++w) rs += rpart[i * WPR + w];
-            dq[((int64_t)bh * n + rc + i) * d + cbase + x] = Elem<T>::store(A(2) * acc - rs);
+            const T v = Elem<T>::store(A(2) * acc - rs);
+            const int64_t o = ((int64_t)bh * n + rc + i) * d + cbase + x;
+            dq[o] = v;
+            for (int p = 0; p < geo.ndqx; ++p) static_cast<T*>(geo.dqx[p])[o] = v;  // peer gather buffers
         }
     }
 
@@ -1493,6 +1507,9 @@ int launch_bwd_wide_flat(const T* g, const T* q, const T* kT, T* dq, T* dk, int6
     BwdGeom geo;
     geo.n = (int)n; geo.m = (int)m; geo.d = (int)d;
     geo.km = fz.km; geo.kscale = fz.kscale;
+    if (fz.ndqx < 0 || fz.ndqx > LF_MAX_PEERS) { set_error("at most %d dQ peers", LF_MAX_PEERS); return LF_ERR_INVALID; }
+    geo.ndqx = fz.ndqx;
+    for (int p = 0; p < fz.ndqx; ++p) geo.dqx[p] = fz.dqx[p];
     geo.DBC = DBT; geo.MCN = MCNT; geo.RG = RG; geo.MP = MPT; geo.RC = RC;
     geo.KSTR = (int)(m | 1);
     geo.rows_per_cta = 0;
@@ -1855,6 +1872,41 @@ extern "C" int lf_laplace_sub_bwd_ws(const void* g, const void* q, const void* k
     LF_DISPATCH(dtype, T, return launch_bwd_flat_t<T>(g, q, kT, dq, dkT, bh, n, m, d, workspace, workspace_bytes,
                                                       nullptr, st));
     return LF_OK;
+}
+
+// lf_laplace_sub_bwd_ws with dQ also stored into peer gather buffers: from
+// inside the balanced wide kernel where it runs, else by a put afterwards.
+extern "C" int lf_laplace_sub_bwd_peers(const void* g, const void* q, const void* kT, void* dq, void* dkT,
+                                        void* const* dq_peers, int npeer, int64_t bh, int64_t n, int64_t m,
+                                        int64_t d, int dtype, void* workspace, size_t workspace_bytes,
+                                        lf_stream_t stream) {
+    clear_error();
+    if (npeer < 0 || npeer > LF_MAX_PEERS || (npeer > 0 && !dq_peers)) {
+        set_error("lf_laplace_sub_bwd_peers: %d peers (at most %d, table required)", npeer, LF_MAX_PEERS);
+        return LF_ERR_INVALID;
+    }
+    for (int p = 0; p < npeer; ++p)
+        if (!dq_peers[p]) { set_error("lf_laplace_sub_bwd_peers: null peer %d", p); return LF_ERR_INVALID; }
+    if (!dq || !dkT) { set_error("lf_laplace_sub_bwd_peers: dq and dkT are required"); return LF_ERR_INVALID; }
+    const size_t need = lf_laplace_sub_bwd_workspace_size(bh, n, m, d, dtype);
+    if (npeer > 0 && need > 0 && wide_flat_shape(m, d) && dtype != LF_F64) {
+        int rc = check_args(g, q, kT, bh, n, m, d, dtype);
+        if (rc) return rc;
+        if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 15)) {
+            set_error("LaplaceSubtraction backward: workspace must be a 16-byte aligned device pointer");
+            return LF_ERR_INVALID;
+        }
+        GFuse fz;
+        fz.dqx = dq_peers;
+        fz.ndqx = npeer;
+        cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+        LF_DISPATCH(dtype, T, return launch_bwd_flat_t<T>(g, q, kT, dq, dkT, bh, n, m, d, workspace, workspace_bytes,
+                                                          nullptr, st, fz));
+        return LF_OK;
+    }
+    int rc = lf_laplace_sub_bwd_ws(g, q, kT, dq, dkT, bh, n, m, d, dtype, workspace, workspace_bytes, stream);
+    if (rc || npeer == 0) return rc;
+    return lf_peer_put(dq, (size_t)(bh * n * d) * dtype_size(dtype), dq_peers, npeer, stream);
 }
 
 // Gradients of Kmat = exp(scale * S) (lf_laplace_kernel_fwd) from dKmat, with

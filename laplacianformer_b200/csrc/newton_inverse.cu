@@ -42,6 +42,8 @@ namespace lfb {
 // whose bounded wait expired.  Read and cleared by lf_device_status().
 __device__ int g_ns_status = 0;
 
+int peer_status(bool clear);  // peer.cu
+
 namespace {
 
 constexpr int kTcThreads = 256;            // 8 warps; two CTAs share an SM
@@ -2008,6 +2010,7 @@ extern "C" int lf_device_status(int clear) {
         int z = 0;
         if (cudaMemcpyToSymbol(g_ns_status, &z, sizeof(int)) != cudaSuccess) return check_launch("status clear");
     }
-    return v;
+    const int pv = peer_status(clear != 0);  // the peer barrier's word
+    return v ? v : pv;
 }
 
