@@ -115,29 +115,45 @@ def _flush_buffer(dev):
     return torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
 
 
-def time_steps(step, steps, warmup, flush, stream, prefill_ms=5.0):
+def time_steps(step, steps, warmup, flush, stream, prefill_ms=None):
     """Warm up, then time `steps` calls of step() with events on `stream`.
 
-    A GPU sleep of `prefill_ms` is enqueued before the timed steps so that the
-    host has queued them all before the GPU reaches them (outside the events)."""
+    A GPU sleep is enqueued before the timed steps so that the host has queued
+    them all before the GPU reaches them (outside the events): host launch
+    cost then cannot show up as device time.  If the sleep had already ended
+    when the host finished queueing (the GPU waited on the host), the loop is
+    repeated with a sleep twice as long, up to four times."""
     for _ in range(warmup):
         step()
     torch.cuda.synchronize()
-    if torch.distributed.is_initialized():
-        torch.distributed.barrier()
-    torch.cuda.synchronize()
-    if prefill_ms > 0:
-        torch.cuda._sleep(int(prefill_ms * 2.0e6))  # ~2 GHz SM clock
-    evs = []
-    for _ in range(steps):
-        flush.zero_()
-        a = torch.cuda.Event(enable_timing=True)
-        b = torch.cuda.Event(enable_timing=True)
-        a.record(stream)
-        step()
-        b.record(stream)
-        evs.append((a, b))
-    torch.cuda.synchronize()
+    if prefill_ms is None:
+        prefill_ms = 4.0 + 1.0 * steps  # ~1 ms of host time per step, generous
+    for attempt in range(4):
+        if torch.distributed.is_initialized():
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+        done = torch.cuda.Event()
+        if prefill_ms > 0:
+            torch.cuda._sleep(int(prefill_ms * 2.0e6))  # ~2 GHz SM clock
+        done.record(stream)
+        evs = []
+        for _ in range(steps):
+            flush.zero_()
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            step()
+            b.record(stream)
+            evs.append((a, b))
+        starved = prefill_ms > 0 and done.query()
+        torch.cuda.synchronize()
+        if torch.distributed.is_initialized():
+            flag = torch.tensor([1.0 if starved else 0.0], device=torch.device("cuda", torch.cuda.current_device()))
+            torch.distributed.all_reduce(flag, op=torch.distributed.ReduceOp.MAX)
+            starved = bool(flag.item() > 0)
+        if not starved or prefill_ms <= 0:
+            break
+        prefill_ms *= 2
     if torch.distributed.is_initialized():
         torch.distributed.barrier()
     return [a.elapsed_time(b) for a, b in evs]

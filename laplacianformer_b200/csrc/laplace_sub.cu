@@ -830,7 +830,12 @@ lsub_bwd_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* __res
 // workspace slot 2i (the CTA's first segment) or 2i+1 (its last), and
 // lsub_bwd_dk_finalize adds the slots.  Every CTA-slot of the machine works
 // (a per-(b,h) cluster leaves SMs idle when bh*cs is not a multiple of them).
-template <typename T, int MB, bool DQ, bool DK, bool FLAT>
+//
+// KM: the gradient is dKmat and the staging forms dS = kscale * Kmat * dKmat
+// (BwdGeom::km); a separate instantiation, so the plain backward carries no
+// trace of it (a runtime test in the staging loads cost the configuration-2
+// backward 40 % of its speed).
+template <typename T, int MB, bool DQ, bool DK, bool FLAT, bool KM>
 __global__ void __launch_bounds__(kThreads, 1)
 lsub_bwd_fast_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* __restrict__ kT,
                      T* __restrict__ dq, T* __restrict__ dk, BwdGeom geo, float* __restrict__ ws) {
@@ -894,9 +899,12 @@ lsub_bwd_fast_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* 
         const int64_t row = rc + sr;
         const bool ok = row < r_end;
         const T* grow = Gb + row * m + sq * CPT;
-        const T* kmrow = geo.km ? static_cast<const T*>(geo.km) + (grow - g) : nullptr;
+        const T* kmrow = KM ? static_cast<const T*>(geo.km) + (grow - g) : nullptr;
 #pragma unroll
-        for (int k = 0; k < CPT; ++k) pg[k] = (ok && sq * CPT + k < m) ? grad_at<T>(grow, kmrow, geo.kscale, k) : A(0);
+        for (int k = 0; k < CPT; ++k) {
+            if constexpr (KM) pg[k] = (ok && sq * CPT + k < m) ? grad_at<T>(grow, kmrow, geo.kscale, k) : A(0);
+            else pg[k] = (ok && sq * CPT + k < m) ? Elem<T>::load(grow[k]) : A(0);
+        }
         const T* qrow = Qb + row * d + sq * 8;
         if (qvec && ok) {  // d == 32, 16-byte aligned rows: the eight values in one or two 16-byte loads
             if constexpr (sizeof(T) == 4) {
@@ -1088,7 +1096,7 @@ int launch_bwd_fast(const T* g, const T* q, const T* kT, T* dq, T* dk, int64_t b
     size_t smem = sizeof(A) * ((size_t)kRowChunk * MB + (size_t)kRowChunk * 32 + kRowChunk + MB +
                                (size_t)32 * geo.KSTR + (size_t)(kThreads / 32) * MB +
                                (DK ? (size_t)(kThreads / 32) * 32 * geo.KSTR : 0));
-    auto kern = lsub_bwd_fast_kernel<T, MB, DQ, DK, false>;
+    auto kern = fz.km ? lsub_bwd_fast_kernel<T, MB, DQ, DK, false, true> : lsub_bwd_fast_kernel<T, MB, DQ, DK, false, false>;
     if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     const int64_t slots = cta_slots(kern, smem);
     const int64_t max_by_rows = (n + kRowChunk - 1) / kRowChunk;
@@ -1139,7 +1147,7 @@ int launch_bwd_flat(const T* g, const T* q, const T* kT, T* dq, T* dk, int64_t b
     size_t smem = sizeof(A) * ((size_t)kRowChunk * MB + (size_t)kRowChunk * 32 + kRowChunk + MB +
                                (size_t)32 * geo.KSTR + (size_t)(kThreads / 32) * MB +
                                (size_t)(kThreads / 32) * 32 * geo.KSTR);
-    auto kern = lsub_bwd_fast_kernel<T, MB, true, true, true>;
+    auto kern = fz.km ? lsub_bwd_fast_kernel<T, MB, true, true, true, true> : lsub_bwd_fast_kernel<T, MB, true, true, true, false>;
     if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     const int64_t slots = cta_slots(kern, smem);
     geo.U = (n + kRowChunk - 1) / kRowChunk;
@@ -1207,7 +1215,7 @@ int launch_bwd_flat_t(const void* g, const void* q, const void* kT, void* dq, vo
 // landmark chunks and dK partials of the row groups are combined in a fixed
 // order (bitwise reproducible); the row-split CTAs of one (b,h) form a
 // cluster and add their dK through distributed shared memory.
-template <typename T, int DBT, int MCNT, int MB, int NT, bool FLAT>
+template <typename T, int DBT, int MCNT, int MB, int NT, bool FLAT, bool KM>
 __global__ void __launch_bounds__(NT, 1)
 lsub_bwd_wide_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* __restrict__ kT,
                      T* __restrict__ dq, T* __restrict__ dk, BwdGeom geo, float* __restrict__ ws) {
@@ -1281,9 +1289,12 @@ lsub_bwd_wide_kernel(const T* __restrict__ g, const T* __restrict__ q, const T* 
 #pragma unroll
         for (int k = 0; k < GPT; ++k) {
             const int64_t row = rc + srow0 + SRS * k;
-            pg[k] = (row < r_end && sj < m)
-                        ? grad_at<T>(Gb, geo.km ? static_cast<const T*>(geo.km) + (Gb - g) : nullptr, geo.kscale, row * m + sj)
-                        : A(0);
+            if constexpr (KM)
+                pg[k] = (row < r_end && sj < m)
+                            ? grad_at<T>(Gb, static_cast<const T*>(geo.km) + (Gb - g), geo.kscale, row * m + sj)
+                            : A(0);
+            else
+                pg[k] = (row < r_end && sj < m) ? Elem<T>::load(Gb[row * m + sj]) : A(0);
         }
 #pragma unroll
         for (int k = 0; k < QPT; ++k) {
@@ -1448,7 +1459,8 @@ int launch_bwd_wide(const T* g, const T* q, const T* kT, T* dq, T* dk, int64_t b
         set_error("LaplaceSubtraction backward: needs %zu bytes of shared memory", smem);
         return LF_ERR_UNSUPPORTED;
     }
-    auto kern = lsub_bwd_wide_kernel<T, DBT, MCNT, MB, NT, false>;
+    auto kern = fz.km ? lsub_bwd_wide_kernel<T, DBT, MCNT, MB, NT, false, true>
+                      : lsub_bwd_wide_kernel<T, DBT, MCNT, MB, NT, false, false>;
     if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     const int64_t slots = cta_slots(kern, smem, NT);
     const int64_t max_by_rows = (n + RC - 1) / RC;
@@ -1520,7 +1532,8 @@ int launch_bwd_wide_flat(const T* g, const T* q, const T* kT, T* dq, T* dk, int6
         set_error("LaplaceSubtraction backward: needs %zu bytes of shared memory", smem);
         return LF_ERR_UNSUPPORTED;
     }
-    auto kern = lsub_bwd_wide_kernel<T, DBT, MCNT, MB, NT, true>;
+    auto kern = fz.km ? lsub_bwd_wide_kernel<T, DBT, MCNT, MB, NT, true, true>
+                      : lsub_bwd_wide_kernel<T, DBT, MCNT, MB, NT, true, false>;
     if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     const int64_t slots = cta_slots(kern, smem, NT);
     geo.U = (n + kRowChunk - 1) / kRowChunk;
