@@ -443,7 +443,7 @@ __device__ __forceinline__ void issue_y(uint32_t acc, uint64_t dah, uint64_t dal
 template <typename T>
 __global__ void __launch_bounds__(kTcThreads, 2)
 ns_tc_fwd_kernel(const T* __restrict__ a, T* __restrict__ x, int batch, int n, int nb, int iters, int mode,
-                 float reg, int precision, const float* __restrict__ lmk, int ld, float lscale) {
+                 float reg, int precision, const float* __restrict__ lmk, int ld, float lscale, int pf_ahead) {
     extern __shared__ __align__(16) unsigned char smem_raw[];  // re-aligned to 1024 below
     // V hi at [0, 32K), V lo at [32K, 64K), G hi at [64K, 96K) of the aligned
     // base; addresses are recomputed from the base where they are used, so
@@ -536,9 +536,42 @@ ns_tc_fwd_kernel(const T* __restrict__ a, T* __restrict__ x, int batch, int n, i
     } else {
         // Gather: warp w covers tile rows w, w+8, ...; lane l columns 4l..4l+3.
         const T* A = a + m0 * (int64_t)n * n;
+        if (tid == 0 && pf_ahead > 0 && (int64_t)blockIdx.x + pf_ahead < (int64_t)gridDim.x) {
+            // Warm L2 with the tile of the CTA that follows `pf_ahead` slots
+            // later (the next wave): its gather then reads L2, not HBM.
+            const int64_t t = (int64_t)blockIdx.x + pf_ahead;
+            const int64_t mt = min((int64_t)nb, (int64_t)batch - t * nb);
+            const uintptr_t lo = (reinterpret_cast<uintptr_t>(a + t * nb * (int64_t)n * n) + 15) & ~uintptr_t(15);
+            const uintptr_t hi = reinterpret_cast<uintptr_t>(a + (t * nb + mt) * (int64_t)n * n) & ~uintptr_t(15);
+            for (uintptr_t p = lo; p < hi; p += 32768) {
+                const uint32_t sz = (uint32_t)min((uintptr_t)32768, hi - p);
+                asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(sz) : "memory");
+            }
+        }
+        bool whole = false;  // fp32, n = 128, 16-byte aligned rows: 16 row loads in flight per thread
+        if constexpr (sizeof(T) == 4) whole = n == kTile && (reinterpret_cast<uintptr_t>(A) & 15) == 0;
+        if (whole) {
+            float4 v[kTile / 8];
+#pragma unroll
+            for (int it = 0; it < kTile / 8; ++it)
+                v[it] = __ldg(reinterpret_cast<const float4*>(A + (int64_t)(warp + 8 * it) * kTile) + lane);
+#pragma unroll
+            for (int it = 0; it < kTile / 8; ++it) {
+                const int i = warp + 8 * it;
+                float4 w = v[it];
+                if ((i >> 2) == lane) {  // the diagonal: column i = component i & 3 (= warp & 3) of lane i / 4
+                    const int q = warp & 3;
+                    w.x += q == 0 ? reg : 0.f;
+                    w.y += q == 1 ? reg : 0.f;
+                    w.z += q == 2 ? reg : 0.f;
+                    w.w += q == 3 ? reg : 0.f;
+                }
+                stage_st4(stage, i, lane, w);
+            }
+        }
         int b = warp / n, r = warp - (warp / n) * n;  // matrix and row within it of tile row `warp`
 #pragma unroll 4
-        for (int it = 0; it < kTile / 8; ++it) {
+        for (int it = 0; it < (whole ? 0 : kTile / 8); ++it) {
             const int i = warp + 8 * it;
             float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
             if (i < nrows) {
@@ -568,8 +601,13 @@ ns_tc_fwd_kernel(const T* __restrict__ a, T* __restrict__ x, int batch, int n, i
 
     // ---- per-matrix statistics (rows and columns of the tile are the
     // thread's `row` index; the two column halves meet in shared memory) ------
+    // Column |.| sums: warp w adds tile rows w, w+8, ... of lane l's columns
+    // 4l..4l+3 into colp[w] (in the V hi region, free until V0 is stored);
+    // the eight partials are added in warp order below.  The same order for
+    // every input path, so the landmark-fused form stays bit-identical.
+    float* colp = reinterpret_cast<float*>(base);  // [8][kTile]
     {
-        float rs = 0.f, ra = 0.f, pm = 0.f, cs = 0.f;
+        float rs = 0.f, ra = 0.f, pm = 0.f;
 #pragma unroll 4
         for (int c4 = 0; c4 < 16; ++c4) {
             const float4 p = stage_ld4(stage, row, 16 * half + c4);
@@ -577,19 +615,25 @@ ns_tc_fwd_kernel(const T* __restrict__ a, T* __restrict__ x, int batch, int n, i
             ra += (fabsf(p.x) + fabsf(p.y)) + (fabsf(p.z) + fabsf(p.w));
             pm = fmaxf(pm, fmaxf(fmaxf(fabsf(p.x), fabsf(p.y)), fmaxf(fabsf(p.z), fabsf(p.w))));
         }
+        float4 cp = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 8
-        for (int i = 64 * half; i < 64 * half + 64; ++i) cs += fabsf(stage[stage_idx(i, row)]);
+        for (int it = 0; it < kTile / 8; ++it) {
+            const float4 p = stage_ld4(stage, warp + 8 * it, lane);
+            cp.x += fabsf(p.x); cp.y += fabsf(p.y); cp.z += fabsf(p.z); cp.w += fabsf(p.w);
+        }
+        *reinterpret_cast<float4*>(colp + warp * kTile + 4 * lane) = cp;
         sh.part[half][row][0] = rs;
         sh.part[half][row][1] = ra;
         sh.part[half][row][2] = pm;
-        sh.part[half][row][3] = cs;
     }
     __syncthreads();
     {
         float rs = sh.part[0][row][0] + sh.part[1][row][0];
         float ra = sh.part[0][row][1] + sh.part[1][row][1];
         float pm = fmaxf(sh.part[0][row][2], sh.part[1][row][2]);
-        float cs = sh.part[0][row][3] + sh.part[1][row][3];
+        float cs = colp[row];
+#pragma unroll
+        for (int w = 1; w < 8; ++w) cs += colp[w * kTile + row];
         rs = seg_max(rs, seg);
         ra = seg_max(ra, seg);
         pm = seg_max(pm, seg);
@@ -1802,8 +1846,10 @@ int launch_tc(const T* a, T* x, int64_t batch, int64_t n, int iters, int mode, f
     auto kern = ns_tc_fwd_kernel<T>;
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    // L2 prefetch distance: the CTA slots of the device (two per SM), i.e. one wave ahead
+    const int pf = lmk ? 0 : 2 * num_sms();
     kern<<<(unsigned)tiles, kTcThreads, smem, st>>>(a, x, (int)batch, (int)n, nb, iters, mode, reg, precision, lmk,
-                                                    ld, lscale);
+                                                    ld, lscale, pf);
     return check_launch("ns_tc_fwd_kernel");
 }
 
