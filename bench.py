@@ -443,9 +443,13 @@ def run_b200(args, rank, world, dev):
         line["newton_inverse"] = newton_section(dev, args.steps, args.warmup, flush, stream, peaks, peak_kind)
         line["gpu_launches"] += 3 * max(2, args.steps // 2)
     if not args.skip_config5:
-        c5 = config5_record(args, rank, world, dev, args.n_tokens, args.gather if world > 1 else "none", flush)
-        line["config5"] = c5
-        line["gpu_launches"] += c5.pop("launches")
+        for key, ntok in (("config5", args.n_tokens), ("config5_long", args.n_tokens_long)):
+            if ntok <= 0:
+                continue
+            c5 = config5_record(args, rank, world, dev, ntok, args.gather if world > 1 else "none", flush)
+            line[key] = c5
+            line["gpu_launches"] += c5.pop("launches")
+            torch.cuda.empty_cache()
     if world == 1 and not args.skip_config4:
         c4 = config4_record(args, dev, flush, stream)
         line["config4"] = c4
@@ -491,14 +495,22 @@ def config5_record(args, rank, world, dev, n_tokens, gather, flush):
     chunk = -(-(B * H) // world)
     steps = max(3, min(args.steps, 10))
 
+    side = torch.cuda.Stream(dev)
+
     def compute(dq, dk, X, dq_peers=None):
+        # The landmark inverse does not depend on the distances: it runs on a
+        # second stream beside them (its few 4-CTA clusters are latency-bound
+        # and would otherwise leave most SMs idle at the end of the step).
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            capi.laplace_kernel_fwd(Lf, LfT, -1.0 / sigma, out=A)  # exp(-cdist_1 / sigma), S never stored
+            capi.newton_inverse_fwd(A, 10, out=X)
         capi.laplace_sub_fwd(q, kT, s)
         if dq_peers:
             capi.laplace_sub_bwd_peers(ds, q, kT, dq, dk, dq_peers, workspace=ws)
         else:
             capi.laplace_sub_bwd(ds, q, kT, dq, dk, workspace=ws)
-        capi.laplace_kernel_fwd(Lf, LfT, -1.0 / sigma, out=A)  # exp(-cdist_1 / sigma), S never stored
-        capi.newton_inverse_fwd(A, 10, out=X)
+        stream.wait_stream(side)
 
     dq, dk = torch.empty_like(q), torch.empty_like(kT)
     X = torch.empty_like(A)
@@ -752,6 +764,8 @@ def main():
     ap.add_argument("--ns-batch", type=int, default=4096)
     ap.add_argument("--workload", choices=["config2", "config5"], default="config2")
     ap.add_argument("--n-tokens", type=int, default=16384, help="configuration-5 sequence length")
+    ap.add_argument("--n-tokens-long", type=int, default=65536,
+                    help="sequence length of the second configuration-5 sub-record (0: leave it out)")
     ap.add_argument("--gather", choices=["none", "after", "peer"], default="peer",
                     help="config 5 with N>1: replicate dQ, dK^T and X on every rank by peer stores from the kernels "
                          "(peer; the NCCL variant is timed beside it), by NCCL after the compute (after), or not at all")
