@@ -40,9 +40,14 @@ def laplacian_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, landm
     D = q.shape[-1]
     sigma = math.sqrt(D) if sigma is None else sigma
     L = landmarks
-    # exp(-S/sigma) is fused into the distance kernel: S is never stored
-    k_ql = laplace_kernel(q, L.transpose(-1, -2).contiguous(), -1.0 / sigma)          # [B,H,N,M]
-    k_lk = laplace_kernel(L, k.transpose(-1, -2).contiguous(), -1.0 / sigma)          # [B,H,M,N]
+    # exp(-S/sigma) is fused into the distance kernel: S is never stored.
+    # K_LK is taken as the transpose of K_KL = exp(-LaplaceSub(K, L^T)/sigma):
+    # |l - k| = |k - l| and the channel sums run in the same order, so it is
+    # bit-identical, and the kernels then work on N query rows per (b,h)
+    # instead of M (M = 49 rows would leave most lanes of a CTA idle).
+    lt = L.transpose(-1, -2).contiguous()
+    k_ql = laplace_kernel(q, lt, -1.0 / sigma)                                        # [B,H,N,M]
+    k_kl = laplace_kernel(k, lt, -1.0 / sigma)                                        # [B,H,N,M] = K_LK^T
     Lf = L.float().contiguous()
     M, D = Lf.shape[-2], Lf.shape[-1]
     if M <= 128 and D <= 128 and precision in (0, 1):
@@ -51,7 +56,7 @@ def laplacian_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, landm
     else:
         k_ll = laplace_kernel(Lf, Lf.transpose(-1, -2).contiguous(), -1.0 / sigma)   # [B,H,M,M] fp32
         x = newton_inverse(k_ll, iters, init_mode=init_mode, precision=precision)
-    kv = k_lk @ v                                                            # [B,H,M,D]
+    kv = k_kl.transpose(-1, -2) @ v                                          # K_LK V: [B,H,M,D]
     return k_ql @ (x.to(q.dtype) @ kv)
 
 
