@@ -722,14 +722,21 @@ ns_tc_fwd_kernel(const T* __restrict__ a, T* __restrict__ x, int batch, int n, i
             // ---- G = I - H (fp16, scaled) into shared memory --------------------
             __half2 hm = __float2half2_rn(0.f);
 #pragma unroll
-            for (int hc = 0; hc < 4; ++hc) {
-                float av[16];
-                tmem_ld16(tmem + tl + c0 + 16 * hc, av);
+            for (int hp = 0; hp < 2; ++hp) {  // two 16-column loads per wait
+                float av[16], aw[16];
+                tmem_ld16(tmem + tl + c0 + 32 * hp, av);
+                tmem_ld16(tmem + tl + c0 + 32 * hp + 16, aw);
                 tmem_wait_ld();
                 reg_fence(av);
+                reg_fence(aw);
                 const uint32_t gh_row = smem_u32(base) + 2 * kOpBytes + rbase;
-                if ((hc >> 1) == dchunk) g_store<true>(av, chs2, sG, lane, 16 * (hc & 1), hm, gh_row, rx, hc);
-                else g_store<false>(av, chs2, sG, lane, 0, hm, gh_row, rx, hc);
+                if (hp == dchunk) {
+                    g_store<true>(av, chs2, sG, lane, 0, hm, gh_row, rx, 2 * hp);
+                    g_store<true>(aw, chs2, sG, lane, 16, hm, gh_row, rx, 2 * hp + 1);
+                } else {
+                    g_store<false>(av, chs2, sG, lane, 0, hm, gh_row, rx, 2 * hp);
+                    g_store<false>(aw, chs2, sG, lane, 0, hm, gh_row, rx, 2 * hp + 1);
+                }
             }
             float gm = seg_max_nn(fmaxf(__low2float(hm), __high2float(hm)), seg, warp_one);
             if (leader) atomicMax(&sh.gmax[par][blk], __float_as_uint(gm));
@@ -757,14 +764,14 @@ ns_tc_fwd_kernel(const T* __restrict__ a, T* __restrict__ x, int batch, int n, i
             tc_fence_after();
             // ---- V <- V + Y ------------------------------------------------------
 #pragma unroll
-            for (int hc = 0; hc < 8; ++hc) {
-                float av[8];
-                tmem_ld8(tmem + tl + c0 + 8 * hc, av);
+            for (int hc = 0; hc < 4; ++hc) {
+                float av[16];
+                tmem_ld16(tmem + tl + c0 + 16 * hc, av);
                 tmem_wait_ld();
                 reg_fence(av);
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int j = 8 * hc + 2 * e;
+                for (int e = 0; e < 8; ++e) {
+                    const int j = 16 * hc + 2 * e;
                     upk2(fma2(pk2(av[2 * e], av[2 * e + 1]), cy2, pk2(V[j], V[j + 1])), V[j], V[j + 1]);
                 }
             }
