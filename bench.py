@@ -248,6 +248,37 @@ def cpu_baseline_eager(w, threads, budget_s=8.0):
                       f"{el:.1f} s"}
 
 
+def packed_fp16_record(dev, steps, warmup, flush, stream, issue_peak):
+    """Configuration 2 forward in fp16: the bit-exact kernel (fp32 arithmetic,
+    2 FP32 instructions per term) beside the opt-in packed-half2 kernel (one
+    HSUB2 + one HADD2 per two terms), with its largest relative error against
+    the bit-exact result on the same inputs."""
+    from laplacianformer_b200 import capi, workloads
+
+    w = workloads.config2(device=dev, dtype=torch.float16)
+    q, kT = w["q"], w["kT"]
+    B, H, N, D = q.shape
+    M = kT.shape[-1]
+    terms = B * H * N * M * D
+    s_exact = torch.empty(B, H, N, M, device=dev, dtype=torch.float16)
+    s_packed = torch.empty_like(s_exact)
+    out = {}
+    for name, fn, s_out in (("exact", capi.laplace_sub_fwd, s_exact), ("packed", capi.laplace_sub_fwd_packed, s_packed)):
+        ms = statistics.mean(time_steps(lambda: fn(q, kT, s_out), steps, warmup, flush, stream))
+        out[name] = {"ms": ms, "gterms_per_s": terms / (ms / 1e3) / 1e9,
+                     "kernel": "lsub_fwd_kernel<__half>" if name == "exact" else "lsub_fwd_h2_kernel"}
+    torch.cuda.synchronize()
+    rel = ((s_packed.float() - s_exact.float()).abs() / s_exact.float().abs().clamp_min(1e-3)).max().item()
+    out["packed"]["max_rel_err_vs_exact"] = rel
+    # instruction-issue roofline: the exact kernel issues 2 FP32-pipe instructions
+    # per term, the packed one 1 (two packed-half2 instructions per two terms)
+    out["exact"]["frac_of_issue"] = 2 * terms / (out["exact"]["ms"] / 1e3) / issue_peak
+    out["packed"]["frac_of_issue"] = 1 * terms / (out["packed"]["ms"] / 1e3) / issue_peak
+    out["workload"] = "config2 forward, fp16 Q [32,2,3136,32], K^T [32,2,32,49]"
+    out["issue_peak"] = "148 SMs x 128 lanes x sampled clock; exact: 2 FP32 instructions per term, packed: 1 per term"
+    return out
+
+
 def newton_section(dev, steps, warmup, flush, stream, peaks, peak_kind):
     """Configuration 3: 4096 SPD 128x128 matrices, 12 iterations, fp32:
     scaled-transpose init in split3 and mixed arithmetic, and the drop-in
@@ -450,6 +481,9 @@ def run_b200(args, rank, world, dev):
             line[key] = c5
             line["gpu_launches"] += c5.pop("launches")
             torch.cuda.empty_cache()
+    if world == 1:
+        line["packed_fp16"] = packed_fp16_record(dev, args.steps, args.warmup, flush, stream, issue_peak)
+        line["gpu_launches"] += 2 * args.steps
     if world == 1 and not args.skip_config4:
         c4 = config4_record(args, dev, flush, stream)
         line["config4"] = c4

@@ -103,6 +103,16 @@ LF_API int lf_laplace_sub_fwd(const void* q, const void* kT, void* s,
                        int64_t bh, int64_t n, int64_t m, int64_t d,
                        int dtype, lf_stream_t stream);
 
+/* lf_laplace_sub_fwd for fp16 storage with packed half2 arithmetic: the
+   differences and 16-channel partial sums are fp16 pairs, the partials are
+   added in fp32.  Opt-in and not bit-identical: within ~1e-3 relative of the
+   fp32 channel sum (the half-precision tolerance of the path is 1e-2).
+   fp16 only (LF_ERR_DTYPE otherwise), d <= 64.  No counterpart in the
+   reference (its half path converts to fp32, LaplaceSubtraction_cuda_kernel.cu:471). */
+LF_API int lf_laplace_sub_fwd_packed(const void* q, const void* kT, void* s,
+                       int64_t bh, int64_t n, int64_t m, int64_t d,
+                       int dtype, lf_stream_t stream);
+
 /* Laplacian kernel matrix Kmat[b,i,j] = exp(scale * S[b,i,j]) with S as in
    lf_laplace_sub_fwd (the same bit-exact channel sums), the exponential
    applied in the accumulation type before the one rounding to the storage

@@ -22,7 +22,7 @@ INCLUDE = os.path.join(ROOT, "include")
 OBJDIR = os.path.join(ROOT, "_build", "capi")
 LIB = os.path.join(PKG, "liblfb200.so")
 
-CU_SOURCES = ["capi.cu", "laplace_sub.cu", "newton_inverse.cu", "host_pipeline.cu", "peer.cu"]
+CU_SOURCES = ["capi.cu", "laplace_sub.cu", "laplace_sub_packed.cu", "newton_inverse.cu", "host_pipeline.cu", "peer.cu"]
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-std=c++17", "-lineinfo",

@@ -33,6 +33,7 @@ SIGNATURES = {
     "lf_cudart_version": (_I, []),
     "lf_version": (_I, []),
     "lf_laplace_sub_fwd": (_I, [_P, _P, _P, _I64, _I64, _I64, _I64, _I, _P]),
+    "lf_laplace_sub_fwd_packed": (_I, [_P, _P, _P, _I64, _I64, _I64, _I64, _I, _P]),
     "lf_laplace_kernel_fwd": (_I, [_P, _P, _P, _I64, _I64, _I64, _I64, _I, _D, _P]),
     "lf_laplace_kernel_bwd": (_I, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I, _D, _P, ctypes.c_size_t, _P]),
     "lf_laplace_sub_bwd_query": (_I, [_P, _P, _P, _P, _I64, _I64, _I64, _I64, _I, _P]),
@@ -133,6 +134,18 @@ def laplace_sub_fwd(q, kT, out=None):
         out = torch.empty(q.shape[0], q.shape[1], n, m, device=q.device, dtype=q.dtype)
     _check(lib().lf_laplace_sub_fwd(_ptr(q), _ptr(kT), _ptr(out), bh, n, m, d, dtype_code(q), _stream(q)),
            "lf_laplace_sub_fwd")
+    return out
+
+
+def laplace_sub_fwd_packed(q, kT, out=None):
+    """Opt-in fp16 forward in packed half2 arithmetic (within ~1e-3 relative,
+    not bit-identical); fp16 tensors only, d <= 64."""
+    _need_cuda(q, kT, out)
+    bh, n, m, d = _dims(q, kT)
+    if out is None:
+        out = torch.empty(q.shape[0], q.shape[1], n, m, device=q.device, dtype=q.dtype)
+    _check(lib().lf_laplace_sub_fwd_packed(_ptr(q), _ptr(kT), _ptr(out), bh, n, m, d, dtype_code(q), _stream(q)),
+           "lf_laplace_sub_fwd_packed")
     return out
 
 

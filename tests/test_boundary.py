@@ -51,6 +51,10 @@ def test_host_only_entry_points():
     assert L.lf_laplace_sub_fwd(None, None, None, -1, 2, 3, 4, 0, None) == capi.LF_ERR_INVALID
     assert L.lf_newton_inverse_fwd(None, None, 1, 257, 3, 0, None) == capi.LF_ERR_UNSUPPORTED
     assert L.lf_newton_inverse_fwd_ex(None, None, 1, 4, 3, 0, 7, 0.0, 0, None) == capi.LF_ERR_INVALID
+    # the packed forward is fp16 only and d <= 64
+    assert L.lf_laplace_sub_fwd_packed(None, None, None, 1, 2, 3, 4, capi.LF_F32, None) == capi.LF_ERR_DTYPE
+    assert L.lf_laplace_sub_fwd_packed(None, None, None, 1, 2, 3, 4, capi.LF_F16, None) == capi.LF_ERR_INVALID
+    assert L.lf_laplace_sub_fwd_packed(None, None, None, 0, 2, 3, 4, capi.LF_F16, None) == capi.LF_OK
     # empty problems are no-ops
     assert L.lf_laplace_sub_fwd(None, None, None, 0, 2, 3, 4, 0, None) == capi.LF_OK
     assert L.lf_newton_inverse_fwd(None, None, 0, 64, 3, 0, None) == capi.LF_OK

@@ -457,3 +457,35 @@ def test_laplace_kernel_autograd_uses_fused_backward(cuda):
     ref.backward(g.double())
     torch.testing.assert_close(qd.grad.double().cpu(), q2.grad, rtol=0, atol=1e-5 * q2.grad.abs().max().item())
     torch.testing.assert_close(kd.grad.double().cpu(), k2.grad, rtol=0, atol=1e-5 * k2.grad.abs().max().item())
+
+
+@pytest.mark.parametrize("shape", [(2, 2, 70, 32, 49), (1, 3, 33, 17, 5), (1, 1, 1, 1, 1), (1, 2, 600, 64, 64),
+                                   (1, 1, 300, 16, 196), (1, 2, 300, 64, 256), (2, 1, 77, 40, 131),
+                                   (32, 2, 3136, 32, 49)], ids=str)
+def test_packed_fp16_forward_within_half_tolerance(cuda, shape):
+    """The opt-in packed-half2 forward against the oracle's fp32 channel sums
+    of the same fp16 inputs: relative error within the 1e-2 of the
+    half-precision path (measured ~1e-3), exact zeros where q = k."""
+    q, k, _ = _inputs(shape, torch.float16, seed=3)
+    s = capi.laplace_sub_fwd_packed(q.cuda(), k.cuda())
+    torch.cuda.synchronize()
+    ref = np.asarray(O.laplace_fwd(q.float(), k.float()), dtype=np.float64)  # fp32 sums of the fp16 values
+    got = s.double().cpu().numpy()
+    assert np.all(np.abs(got - ref) <= 1e-2 * np.abs(ref) + 1e-3), np.max(np.abs(got - ref) / (np.abs(ref) + 1e-3))
+    # the same query rows as landmarks give zero distances on the diagonal
+    B, H, N, D, M = shape
+    if N >= M:
+        kq = q[:, :, :M, :].transpose(-1, -2).contiguous()
+        s2 = capi.laplace_sub_fwd_packed(q.cuda(), kq.cuda())
+        torch.cuda.synchronize()
+        diag = torch.diagonal(s2[:, :, :M, :], dim1=-2, dim2=-1)
+        assert torch.all(diag == 0)
+
+
+def test_packed_fp16_forward_rejects_other_dtypes(cuda):
+    q, k, _ = _inputs((1, 1, 8, 8, 4), torch.float32)
+    with pytest.raises(RuntimeError):
+        capi.laplace_sub_fwd_packed(q.cuda(), k.cuda())
+    q, k, _ = _inputs((1, 1, 8, 65, 4), torch.float16)
+    with pytest.raises(RuntimeError):
+        capi.laplace_sub_fwd_packed(q.cuda(), k.cuda())
