@@ -316,15 +316,17 @@ def newton_section(dev, steps, warmup, flush, stream, peaks, peak_kind):
                          "issued_products_per_iteration": units,
                          "issued_tensor_tflops": units / 2.0 * ach,
                          "issued_frac": units / 2.0 * ach / peaks["bf16_tflops"],
-                         "traffic": None},
+                         "traffic": NCU_TRAFFIC["ns_tc_fwd_kernel"] if name == "split3" else None,
+                         "algorithmic_bytes_per_launch": batch * 2 * 128 * 128 * 4},
         }
     return out
 
 
-# DRAM bytes of one launch of each configuration-2 fp32 kernel, from the ncu
-# capture summarised in profiles/laplace_sub_config2_fp32.md
-# (dram__bytes_read.sum + dram__bytes_write.sum).
-NCU_TRAFFIC = {"lsub_bwd_fast_kernel": 65.5e6 + 5.2e6, "lsub_fwd_kernel": 26.1e6 + 0.29e6}
+# DRAM bytes of one launch of each kernel, from the ncu captures summarised
+# under profiles/ (dram__bytes_read.sum + dram__bytes_write.sum).
+NCU_TRAFFIC = {"lsub_bwd_fast_kernel": 65.50e6 + 1.96e6, "lsub_fwd_kernel": 26.15e6 + 0.13e6,
+               # the 4096-matrix configuration-3 launch, split3 (the written X partly still in L2 at exit)
+               "ns_tc_fwd_kernel": 268.9e6 + 217.0e6}
 
 
 def copy_bound_ms(hin, din, hout, dout, steps, dev):
@@ -354,6 +356,17 @@ def copy_bound_ms(hin, din, hout, dout, steps, dev):
 
 
 def run_b200(args, rank, world, dev):
+    # Clocks over every timed region of the run (the headline loop alone is a
+    # few ms, shorter than one nvidia-smi sample period).
+    with ClockSampler(dev.index) as clk_all:
+        line = _run_b200(args, rank, world, dev)
+    line["clocks_headline_loop"] = line.pop("clocks")
+    line["clocks"] = clk_all.summary()
+    line["clocks"]["scope"] = "sampled every 200 ms from before the first warm-up to after the last record"
+    return line
+
+
+def _run_b200(args, rank, world, dev):
     from laplacianformer_b200 import capi, workloads
 
     peaks, peak_kind = _peaks()
