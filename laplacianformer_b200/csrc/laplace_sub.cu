@@ -197,12 +197,17 @@ __device__ __forceinline__ A fwd_epilogue(A acc, A escale, bool do_exp) {
 // |0 - 0| = +0, which leaves every sum unchanged); otherwise the channels are
 // walked in DR-wide chunks.  ks holds KT transposed to [m][DP] in the
 // accumulation type (DP = max(DR, d rounded up to 16), zero padded).
+// Landmark windows: CTA (x, y) computes landmarks [y*mwin, y*mwin + m) of
+// its rows (m = min(mwin, mfull - y*mwin)); mfull is the row stride of S
+// and K^T.  More, smaller CTAs fill the last wave of a small grid better.
 template <typename T, int TM, int MC, int DR>
 __global__ void __launch_bounds__(kThreads)
 lsub_fwd_kernel(const T* __restrict__ q, const T* __restrict__ kT, T* __restrict__ s,
-                int n, int m, int d, int tiles_per_bh, bool vec, int gw,
+                int n, int mfull, int mwin, int d, int tiles_per_bh, bool vec, int gw,
                 typename Elem<T>::acc escale, bool do_exp) {
     using A = typename Elem<T>::acc;
+    const int j_off = (int)blockIdx.y * mwin;
+    const int m = min(mwin, mfull - j_off);
     extern __shared__ __align__(16) unsigned char smem_raw[];
     A* ks = reinterpret_cast<A*>(smem_raw);
     const int d16 = (d + 15) & ~15;
@@ -218,18 +223,18 @@ lsub_fwd_kernel(const T* __restrict__ q, const T* __restrict__ kT, T* __restrict
 
     const int bh = blockIdx.x / tiles_per_bh;
     const int tile = blockIdx.x - bh * tiles_per_bh;
-    const T* Kb = kT + (int64_t)bh * d * m;
+    const T* Kb = kT + (int64_t)bh * d * mfull + j_off;
 
     // Stage KT[bh] (d x m, row-major) transposed into ks[j][c].
     for (int e = threadIdx.x; e < MP * DP; e += kThreads) {
         int j = e / DP, c = e - j * DP;
-        ks[e] = (j < m && c < d) ? Elem<T>::load(Kb[(int64_t)c * m + j]) : A(0);
+        ks[e] = (j < m && c < d) ? Elem<T>::load(Kb[(int64_t)c * mfull + j]) : A(0);
     }
     __syncthreads();
 
     const int64_t row0 = (int64_t)tile * (kThreads * TM) + threadIdx.x;
     const T* Qb = q + (int64_t)bh * n * d;
-    T* Sb = s + (int64_t)bh * n * m;
+    T* Sb = s + (int64_t)bh * n * mfull + j_off;
 
     A qr[TM][DR];
     auto load_q = [&](int dc) {
@@ -295,7 +300,7 @@ lsub_fwd_kernel(const T* __restrict__ q, const T* __restrict__ kT, T* __restrict
             }
             int64_t row = row0 + (int64_t)kThreads * r;
             if (row >= n) continue;
-            T* out = Sb + row * m + mc;
+            T* out = Sb + row * mfull + mc;
 #pragma unroll
             for (int j = 0; j < MC; ++j)
                 if (mc + j < m) out[j] = Elem<T>::store(fwd_epilogue(acc[r][j], escale, do_exp));
@@ -304,7 +309,7 @@ lsub_fwd_kernel(const T* __restrict__ q, const T* __restrict__ kT, T* __restrict
             __syncthreads();
             const int w = (m - g0) < gw ? (m - g0) : gw;
             constexpr int V = 16 / sizeof(T);
-            if (w == m) {
+            if (w == m && m == mfull) {
                 // the tile's rows are one contiguous run of S
                 const int64_t cnt = rows * m;
                 T* dst = Sb + trow * m;
@@ -318,22 +323,22 @@ lsub_fwd_kernel(const T* __restrict__ q, const T* __restrict__ kT, T* __restrict
                 }
                 for (int64_t e = head + threadIdx.x; e < cnt; e += kThreads) dst[e] = so[e];
             } else {
-                T* dst = Sb + trow * m + g0;
-                const bool v16 = (w % V == 0) && (m % V == 0) && (gw % V == 0) &&
+                T* dst = Sb + trow * mfull + g0;
+                const bool v16 = (w % V == 0) && (mfull % V == 0) && (gw % V == 0) &&
                                  (reinterpret_cast<uintptr_t>(dst) & 15) == 0;
                 if (v16) {
                     const int U = w / V;
                     for (int64_t e = threadIdx.x; e < rows * U; e += kThreads) {
                         const int64_t r = e / U;
                         const int u = (int)(e - r * U);
-                        *reinterpret_cast<uint4*>(dst + r * m + u * V) =
+                        *reinterpret_cast<uint4*>(dst + r * mfull + u * V) =
                             *reinterpret_cast<const uint4*>(so + r * gw + u * V);
                     }
                 } else {
                     for (int64_t e = threadIdx.x; e < rows * w; e += kThreads) {
                         const int64_t r = e / w;
                         const int cc = (int)(e - r * w);
-                        dst[r * m + cc] = so[r * gw + cc];
+                        dst[r * mfull + cc] = so[r * gw + cc];
                     }
                 }
             }
@@ -389,38 +394,62 @@ size_t fwd_smem_total(int64_t m, int64_t d) {
 template <typename T, int TM, int MC, int DR>
 int launch_fwd_mc(const T* q, const T* kT, T* s, int64_t bh, int64_t n, int64_t m, int64_t d,
                   cudaStream_t st, double escale, bool do_exp) {
-    size_t smem = fwd_smem_total<T, TM, MC, DR>(m, d);
-    int gw = fwd_stage_width<T, TM, MC>(m);
-    {
+    auto kern = lsub_fwd_kernel<T, TM, MC, DR>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, max_optin_smem());
+    const int tiles = (int)((n + kThreads * TM - 1) / (kThreads * TM));
+    // Shared memory and staged-output width for landmark windows of mw columns.
+    auto plan = [&](int64_t mw, size_t& smem, int& gw) {
+        smem = fwd_smem_total<T, TM, MC, DR>(mw, d);
+        gw = fwd_stage_width<T, TM, MC>(mw);
         // Narrower landmark groups when that lets two CTAs share an SM (the
         // staged K^T and the output tile of one CTA otherwise fill more than
         // half of its shared memory, leaving 8 warps per SM).
         const size_t half_sm = (size_t)max_optin_smem() / 2 - 1024;
-        const size_t ksb = (fwd_smem<T, TM, MC, DR>(m, d) + 15) & ~(size_t)15;
+        const size_t ksb = (fwd_smem<T, TM, MC, DR>(mw, d) + 15) & ~(size_t)15;
         const size_t row_bytes = (size_t)kThreads * TM * sizeof(T);
         if (gw > 0 && smem > half_sm && ksb + 2 * MC * row_bytes <= half_sm) {
             gw = (int)(((half_sm - ksb) / row_bytes) / MC * MC);
             smem = ksb + (size_t)gw * row_bytes;
         }
-    }
-    if (gw == 0 || smem > (size_t)max_optin_smem()) {
-        gw = 0;
-        smem = fwd_smem<T, TM, MC, DR>(m, d);
+        if (gw == 0 || smem > (size_t)max_optin_smem()) {
+            gw = 0;
+            smem = fwd_smem<T, TM, MC, DR>(mw, d);
+        }
+    };
+    // Landmark windows: 1, 2 or 4 (each a multiple of MC landmarks), chosen
+    // by the estimated time waves x (landmarks per CTA + a query-row load
+    // worth ~MC landmarks); ties keep fewer windows.
+    int64_t mw = m;
+    size_t smem = 0;
+    int gw = 0;
+    plan(m, smem, gw);
+    double best = -1.0;
+    for (int nw = 1; nw <= 4; nw *= 2) {
+        // (one window is exactly m wide: the staged tile is then one contiguous run of S)
+        const int64_t w = nw == 1 ? m : ((m + nw - 1) / nw + MC - 1) / MC * MC;
+        if (nw > 1 && w < 4 * MC) break;
+        const int64_t nwin = (m + w - 1) / w;
+        size_t sm_w;
+        int gw_w;
+        plan(w, sm_w, gw_w);
+        if (sm_w > (size_t)max_optin_smem()) continue;
+        const int64_t slots = cta_slots(kern, sm_w);
+        const int64_t blocks = bh * tiles * nwin;
+        const double est = (double)((blocks + slots - 1) / slots) * (double)(w + MC);
+        if (best < 0 || est < best * 0.97) { best = est; mw = w; smem = sm_w; gw = gw_w; }
     }
     if (smem > (size_t)max_optin_smem()) {
         set_error("LaplaceSubtraction forward: m*d = %lld*%lld needs %zu bytes of shared memory",
                   (long long)m, (long long)d, smem);
         return LF_ERR_UNSUPPORTED;
     }
-    auto kern = lsub_fwd_kernel<T, TM, MC, DR>;
-    if (smem > 48 * 1024)
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    int tiles = (int)((n + kThreads * TM - 1) / (kThreads * TM));
+    const int64_t nwin = (m + mw - 1) / mw;
     int64_t blocks = bh * tiles;
-    if (blocks > 0x7fffffff) { set_error("too many blocks"); return LF_ERR_UNSUPPORTED; }
+    if (blocks > 0x7fffffff || nwin > 65535) { set_error("too many blocks"); return LF_ERR_UNSUPPORTED; }
     bool vec = (d % 16 == 0) && aligned(q, 16);
-    kern<<<(unsigned)blocks, kThreads, smem, st>>>(q, kT, s, (int)n, (int)m, (int)d, tiles, vec, gw,
-                                                   (typename Elem<T>::acc)escale, do_exp);
+    kern<<<dim3((unsigned)blocks, (unsigned)nwin), kThreads, smem, st>>>(q, kT, s, (int)n, (int)m, (int)mw, (int)d,
+                                                                        tiles, vec, gw,
+                                                                        (typename Elem<T>::acc)escale, do_exp);
     return check_launch("lsub_fwd_kernel");
 }
 
