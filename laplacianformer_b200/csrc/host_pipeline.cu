@@ -26,8 +26,9 @@ struct Plan {
     int64_t per;         // (b,h) slices of the largest chunk
     std::vector<int64_t> start;  // chunk i covers slices [start[i], start[i+1])
     size_t es;
-    size_t q, k, g, s, dq, dk, ws;  // bytes of each region of one set
-    size_t set;                     // bytes of one buffer set
+    size_t q, g, s, dq, ws;  // bytes of each region of one set
+    size_t set;              // bytes of one buffer set
+    size_t kall;             // K^T (and dK^T) of all slices: copied in once, out once
 };
 
 Plan make_plan(int64_t bh, int64_t n, int64_t m, int64_t d, int dtype, int chunks) {
@@ -54,11 +55,10 @@ Plan make_plan(int64_t bh, int64_t n, int64_t m, int64_t d, int dtype, int chunk
     p.per = base;
     p.es = dtype_size(dtype);
     p.q = up((size_t)p.per * n * d * p.es);
-    p.k = up((size_t)p.per * d * m * p.es);
+    p.kall = up((size_t)bh * d * m * p.es);
     p.g = up((size_t)p.per * n * m * p.es);
     p.s = p.g;
     p.dq = p.q;
-    p.dk = p.k;
     // workspace need is not monotonic in the slice count (it follows the
     // balanced backward's grid): take the largest over the chunk widths
     p.ws = 0;
@@ -66,7 +66,7 @@ Plan make_plan(int64_t bh, int64_t n, int64_t m, int64_t d, int dtype, int chunk
         const size_t w = up(lf_laplace_sub_bwd_workspace_size(p.start[i + 1] - p.start[i], n, m, d, dtype));
         if (w > p.ws) p.ws = w;
     }
-    p.set = p.q + p.k + p.g + p.s + p.dq + p.dk + p.ws;
+    p.set = p.q + p.g + p.s + p.dq + p.ws;
     return p;
 }
 
@@ -111,7 +111,8 @@ extern "C" size_t lf_laplace_sub_host_buffer_size(int64_t bh, int64_t n, int64_t
                                                   int chunks) {
     clear_error();
     if (bh <= 0 || n < 0 || m < 0 || d < 0 || dtype_size(dtype) == 0) return 0;
-    return make_plan(bh, n, m, d, dtype, chunks).set * kRing;
+    const Plan p = make_plan(bh, n, m, d, dtype, chunks);
+    return p.set * kRing + 2 * p.kall;
 }
 
 extern "C" int lf_laplace_sub_fwd_bwd_host(const void* hq, const void* hkT, const void* hg, void* hs, void* hdq,
@@ -130,8 +131,9 @@ extern "C" int lf_laplace_sub_fwd_bwd_host(const void* hq, const void* hkT, cons
         return LF_ERR_INVALID;
     }
     const Plan p = make_plan(bh, n, m, d, dtype, chunks);
-    if (dbuf_bytes < p.set * kRing) {
-        set_error("lf_laplace_sub_fwd_bwd_host: device buffer of %zu bytes, %zu needed", dbuf_bytes, p.set * kRing);
+    if (dbuf_bytes < p.set * kRing + 2 * p.kall) {
+        set_error("lf_laplace_sub_fwd_bwd_host: device buffer of %zu bytes, %zu needed", dbuf_bytes,
+                  p.set * kRing + 2 * p.kall);
         return LF_ERR_INVALID;
     }
     int dev = 0;
@@ -161,23 +163,28 @@ extern "C" int lf_laplace_sub_fwd_bwd_host(const void* hq, const void* hkT, cons
     LF_TRY(cudaStreamWaitEvent(S.run, S.start, 0), "cudaStreamWaitEvent");
     LF_TRY(cudaStreamWaitEvent(S.out, S.start, 0), "cudaStreamWaitEvent");
     const int64_t nchunks = (int64_t)p.start.size() - 1;
+    // K^T is small (d x m per slice): one copy in before the chunks and one
+    // copy of dK^T out after them, instead of two small copies per chunk
+    // (each costs a fixed ~10 us of the copy engines' time).
+    char* kall = base + (size_t)kRing * p.set;
+    char* dkall = kall + p.kall;
+    LF_TRY(cudaMemcpyAsync(kall, Hk, (size_t)bh * d * m * es, cudaMemcpyHostToDevice, S.in), "copy-in");
     for (int64_t i = 0; i < nchunks; ++i) {
         const int r = (int)(i % kRing);
         const int64_t a = p.start[i];
         const int64_t w = p.start[i + 1] - a;
         char* b = base + (size_t)r * p.set;
         char* dq_in = b;
-        char* dk_in = dq_in + p.q;
-        char* dg_in = dk_in + p.k;
+        char* dg_in = dq_in + p.q;
         char* ds_out = dg_in + p.g;
         char* ddq_out = ds_out + p.s;
-        char* ddk_out = ddq_out + p.dq;
-        char* dws = ddk_out + p.dk;
-        const size_t bq = (size_t)w * n * d * es, bk = (size_t)w * d * m * es, bg = (size_t)w * n * m * es;
+        char* dws = ddq_out + p.dq;
+        char* dk_in = kall + (size_t)a * d * m * es;
+        char* ddk_out = dkall + (size_t)a * d * m * es;
+        const size_t bq = (size_t)w * n * d * es, bg = (size_t)w * n * m * es;
         // copy-in; the set is free once the copy-out kRing chunks back is done
         if (i >= kRing) LF_TRY(cudaStreamWaitEvent(S.in, S.freed[r], 0), "cudaStreamWaitEvent");
         LF_TRY(cudaMemcpyAsync(dq_in, Hq + (size_t)a * n * d * es, bq, cudaMemcpyHostToDevice, S.in), "copy-in");
-        LF_TRY(cudaMemcpyAsync(dk_in, Hk + (size_t)a * d * m * es, bk, cudaMemcpyHostToDevice, S.in), "copy-in");
         LF_TRY(cudaMemcpyAsync(dg_in, Hg + (size_t)a * n * m * es, bg, cudaMemcpyHostToDevice, S.in), "copy-in");
         LF_TRY(cudaEventRecord(S.loaded[r], S.in), "cudaEventRecord");
         // kernels
@@ -193,11 +200,13 @@ extern "C" int lf_laplace_sub_fwd_bwd_host(const void* hq, const void* hkT, cons
         LF_TRY(cudaStreamWaitEvent(S.out, S.done[r], 0), "cudaStreamWaitEvent");
         LF_TRY(cudaMemcpyAsync(Hs + (size_t)a * n * m * es, ds_out, bg, cudaMemcpyDeviceToHost, S.out), "copy-out");
         LF_TRY(cudaMemcpyAsync(Hdq + (size_t)a * n * d * es, ddq_out, bq, cudaMemcpyDeviceToHost, S.out), "copy-out");
-        LF_TRY(cudaMemcpyAsync(Hdk + (size_t)a * d * m * es, ddk_out, bk, cudaMemcpyDeviceToHost, S.out), "copy-out");
         LF_TRY(cudaEventRecord(S.freed[r], S.out), "cudaEventRecord");
     }
-    // the caller's stream continues after the last copy-out (copy-outs are
-    // in stream order, so the last one covers all)
+    // dK^T of every slice (the kernels run in stream order: the last chunk's
+    // completion covers all), then the caller's stream continues after the
+    // last copy-out
+    LF_TRY(cudaMemcpyAsync(Hdk, dkall, (size_t)bh * d * m * es, cudaMemcpyDeviceToHost, S.out), "copy-out");
+    LF_TRY(cudaEventRecord(S.freed[(nchunks - 1) % kRing], S.out), "cudaEventRecord");
     LF_TRY(cudaStreamWaitEvent(st, S.freed[(nchunks - 1) % kRing], 0), "cudaStreamWaitEvent");
     return LF_OK;
 }
